@@ -1,0 +1,262 @@
+// Tile binning: per-Gaussian tile rectangles, order-preserving compaction of the visible
+// Gaussians into depth-sort input, the pair-count total, the depth-ordered pair
+// duplication and the tile ranges.
+//
+// Sort strategy. The reference sorts 64-bit keys (tile << 32 | depth bits) with a stable
+// radix sort over all 64 bits (csrc/forward/rasterize.cu:416-435). An LSD radix sort
+// processes the 32 depth bits before the tile bits, and pair duplication copies a
+// Gaussian's depth bits unchanged into each of its pairs without reordering Gaussians, so
+// the four depth passes can run on the visible Gaussians (N_v items) before duplication
+// instead of on the M pairs after it. Only ceil(log2(T) / 8) passes over the M pairs
+// remain. Ties (equal tile and bit-identical depth) keep Gaussian-index order in both
+// schemes, so the sorted order is identical to the reference's.
+#pragma once
+
+#include "gs_common.cuh"
+
+namespace gs {
+
+constexpr int kBinThreads = 256;
+
+// Packed tile rectangle: x = x0 | x1 << 16, y = y0 | y1 << 16.
+__device__ __forceinline__ uint2 pack_rect(const TileRect& r) {
+  return make_uint2((unsigned)r.x0 | ((unsigned)r.x1 << 16),
+                    (unsigned)r.y0 | ((unsigned)r.y1 << 16));
+}
+
+__device__ __forceinline__ TileRect unpack_rect(uint2 p) {
+  TileRect r;
+  r.x0 = (int)(p.x & 0xffffu);
+  r.x1 = (int)(p.x >> 16);
+  r.y0 = (int)(p.y & 0xffffu);
+  r.y1 = (int)(p.y >> 16);
+  return r;
+}
+
+// Per-Gaussian blend record, 3 x float4:
+//   [0] = (mean.x, mean.y, conic.x, conic.y)
+//   [1] = (conic.z, opacity, r, g)
+//   [2] = (b, gaussian index as bits, 0, 0)
+struct BinParams {
+  int N, W, H, tiles_x, tiles_y;
+  const float* depths;
+  const float* mean2d;
+  const float* cov2d;
+  const float* colors;
+  const float* alpha;
+  uint2* rects;
+  float4* records;
+  unsigned* depth_keys;
+  unsigned* depth_vals;
+  unsigned* status;             // look-back words, one per tile of kBinThreads Gaussians
+  unsigned* ticket;
+  unsigned* done_counter;
+  unsigned* depth_hist;         // [4][256]
+  unsigned long long* pair_acc; // running pair total
+  int* n_visible;
+  int* pair_count;              // M, clamped to INT_MAX
+  long long pair_capacity;
+};
+
+__global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
+  __shared__ unsigned s_tile, s_prefix;
+  __shared__ unsigned s_scan[33];
+  __shared__ unsigned s_hist[4][256];
+  __shared__ bool s_last;
+  const int tid = threadIdx.x;
+  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
+  for (int i = tid; i < 4 * 256; i += kBinThreads) (&s_hist[0][0])[i] = 0u;
+  __syncthreads();
+  const int tile = (int)s_tile;
+  const int i = tile * kBinThreads + tid;
+
+  unsigned count = 0, depth_bits = 0;
+  if (i < p.N) {
+    const float2 mean = make_float2(__ldg(p.mean2d + 2 * i), __ldg(p.mean2d + 2 * i + 1));
+    const float a = __ldg(p.cov2d + 3 * i), b = __ldg(p.cov2d + 3 * i + 1),
+                c = __ldg(p.cov2d + 3 * i + 2);
+    TileRect r;
+    if (splat_tile_rect(mean, a, b, c, p.W, p.H, p.tiles_x, p.tiles_y, r)) {
+      count = (unsigned)rect_count(r);
+      if (count > 0) {
+        p.rects[i] = pack_rect(r);
+        const float3 conic = conic_from_cov(a, b, c);
+        const float op = __ldg(p.alpha + i);
+        const float cr = __ldg(p.colors + 3 * i), cg = __ldg(p.colors + 3 * i + 1),
+                    cb = __ldg(p.colors + 3 * i + 2);
+        p.records[3 * i + 0] = make_float4(mean.x, mean.y, conic.x, conic.y);
+        p.records[3 * i + 1] = make_float4(conic.z, op, cr, cg);
+        p.records[3 * i + 2] = make_float4(cb, __int_as_float(i), 0.0f, 0.0f);
+        depth_bits = __float_as_uint(__ldg(p.depths + i));
+      }
+    }
+  }
+  const unsigned visible = count > 0 ? 1u : 0u;
+
+  // order-preserving compaction of visible Gaussians (decoupled look-back over tiles)
+  unsigned n_vis_tile;
+  const unsigned excl = block_exclusive_scan(visible, s_scan, &n_vis_tile);
+  if (tid == 0)
+    st_relaxed(p.status + tile, (tile == 0 ? kFlagPrefix : kFlagAggregate) | n_vis_tile);
+  if (tid < 32) {
+    unsigned prefix = 0;
+    if (tile > 0) prefix = lookback_warp(p.status, tile);
+    if (tid == 0) {
+      if (tile > 0) st_relaxed(p.status + tile, kFlagPrefix | (prefix + n_vis_tile));
+      s_prefix = prefix;
+    }
+  }
+  unsigned tile_pairs;
+  block_exclusive_scan(count, s_scan, &tile_pairs);  // also orders s_prefix
+  if (visible && s_prefix + excl < (unsigned)p.N) {
+    const unsigned pos = s_prefix + excl;
+    p.depth_keys[pos] = depth_bits;
+    p.depth_vals[pos] = (unsigned)i;
+    atomicAdd(&s_hist[0][depth_bits & 255u], 1u);
+    atomicAdd(&s_hist[1][(depth_bits >> 8) & 255u], 1u);
+    atomicAdd(&s_hist[2][(depth_bits >> 16) & 255u], 1u);
+    atomicAdd(&s_hist[3][depth_bits >> 24], 1u);
+  }
+  __syncthreads();
+  for (int k = tid; k < 4 * 256; k += kBinThreads) {
+    const unsigned h = (&s_hist[0][0])[k];
+    if (h) atomicAdd(p.depth_hist + k, h);
+  }
+  const int num_tiles = (p.N + kBinThreads - 1) / kBinThreads;
+  if (tid == 0) {
+    if (tile_pairs) atomicAdd(p.pair_acc, (unsigned long long)tile_pairs);
+    if (tile == num_tiles - 1) *p.n_visible = (int)(s_prefix + n_vis_tile);
+    __threadfence();
+    s_last = atomicAdd(p.done_counter, 1u) == (unsigned)(num_tiles - 1);
+  }
+  __syncthreads();
+  if (s_last && tid == 0) {
+    // every other tile's pair total is visible after its fence + done_counter increment
+    __threadfence();
+    const unsigned long long m = atomicAdd(p.pair_acc, 0ull);
+    const unsigned long long clamped = m > 0x7fffffffull ? 0x7fffffffull : m;
+    *p.pair_count = (int)clamped;
+    if (m > 0x7fffffffull) raise_device_error(kErrCapacity);
+  }
+}
+
+struct DupParams {
+  int tiles_x;
+  int n_tile_passes;
+  const int* n_visible;
+  const int* pair_count;
+  long long pair_capacity;
+  const unsigned* sorted_gids;  // depth-sorted visible Gaussians
+  const uint2* rects;
+  unsigned* status;
+  unsigned* ticket;
+  unsigned* tile_keys;
+  unsigned* tile_vals;
+  unsigned* tile_hist;  // [n_tile_passes][256]
+};
+
+// Exclusive scan of the tile counts in depth order and duplication of each Gaussian into
+// one (tile id, Gaussian index) pair per covered tile, row-major over its rectangle
+// (the order of csrc/forward/rasterize.cu:124-135). A block's pairs are contiguous, so
+// the block writes them cooperatively: pair p belongs to the Gaussian whose exclusive
+// offset is the last one <= p.
+__global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p) {
+  __shared__ unsigned s_tile, s_prefix;
+  __shared__ unsigned s_scan[33];
+  __shared__ unsigned s_off[kBinThreads];
+  __shared__ uint2 s_rect[kBinThreads];
+  __shared__ unsigned s_gid[kBinThreads];
+  __shared__ unsigned s_hist[4][256];
+  const int tid = threadIdx.x;
+  if ((long long)(*p.pair_count) > p.pair_capacity) return;
+  const int nv = *p.n_visible;
+  const int num_tiles = (nv + kBinThreads - 1) / kBinThreads;
+  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
+  for (int k = tid; k < 4 * 256; k += kBinThreads) (&s_hist[0][0])[k] = 0u;
+  __syncthreads();
+  const int tile = (int)s_tile;
+  if (tile >= num_tiles) return;
+  const int j = tile * kBinThreads + tid;
+  unsigned count = 0, gid = 0;
+  uint2 pr = make_uint2(0u, 0u);
+  if (j < nv) {
+    gid = p.sorted_gids[j];
+    pr = p.rects[gid];
+    count = rect_count(unpack_rect(pr));
+  }
+  unsigned tile_pairs;
+  const unsigned excl = block_exclusive_scan(count, s_scan, &tile_pairs);
+  if (tid == 0)
+    st_relaxed(p.status + tile, (tile == 0 ? kFlagPrefix : kFlagAggregate) | tile_pairs);
+  if (tid < 32) {
+    unsigned prefix = 0;
+    if (tile > 0) prefix = lookback_warp(p.status, tile);
+    if (tid == 0) {
+      if (tile > 0) st_relaxed(p.status + tile, kFlagPrefix | (prefix + tile_pairs));
+      s_prefix = prefix;
+    }
+  }
+  s_off[tid] = excl;
+  s_rect[tid] = pr;
+  s_gid[tid] = gid;
+  __syncthreads();
+  const unsigned base = s_prefix;
+  const unsigned M = (unsigned)*p.pair_count;
+  if (base + tile_pairs > M) {  // only reachable after a look-back timeout
+    if (tid == 0) raise_device_error(kErrBadIndex);
+    return;
+  }
+  for (unsigned q = tid; q < tile_pairs; q += kBinThreads) {
+    // last k with s_off[k] <= q
+    int lo = 0, hi = kBinThreads - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_off[mid] <= q) lo = mid; else hi = mid - 1;
+    }
+    const TileRect r = unpack_rect(s_rect[lo]);
+    const unsigned w = (unsigned)(r.x1 - r.x0);
+    const unsigned lp = q - s_off[lo];
+    const unsigned row = lp / w, col = lp - row * w;
+    const unsigned tile_id = (unsigned)(r.y0 + row) * (unsigned)p.tiles_x + (unsigned)r.x0 + col;
+    p.tile_keys[base + q] = tile_id;
+    p.tile_vals[base + q] = s_gid[lo];
+    for (int pass = 0; pass < p.n_tile_passes; ++pass)
+      atomicAdd(&s_hist[pass][(tile_id >> (8 * pass)) & 255u], 1u);
+  }
+  __syncthreads();
+  for (int k = tid; k < p.n_tile_passes * 256; k += kBinThreads) {
+    const unsigned h = (&s_hist[0][0])[k];
+    if (h) atomicAdd(p.tile_hist + k, h);
+  }
+}
+
+// Tile ranges from the tile-sorted keys (csrc/forward/rasterize.cu:146-165); ranges of
+// tiles with no pairs stay (0, 0) from the preceding memset.
+__global__ void __launch_bounds__(256) tile_ranges_kernel(const unsigned* __restrict__ keys,
+                                                          const int* pair_count,
+                                                          long long pair_capacity,
+                                                          unsigned num_tiles,
+                                                          int2* __restrict__ ranges) {
+  const int M = *pair_count;
+  if ((long long)M > pair_capacity) return;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < M;
+       idx += gridDim.x * blockDim.x) {
+    const unsigned cur = keys[idx];
+    if (cur >= num_tiles || (idx > 0 && keys[idx - 1] >= num_tiles)) {
+      raise_device_error(kErrBadIndex);
+      continue;
+    }
+    if (idx == 0) {
+      ranges[cur].x = 0;
+    } else {
+      const unsigned prev = keys[idx - 1];
+      if (cur != prev) {
+        ranges[prev].y = idx;
+        ranges[cur].x = idx;
+      }
+    }
+    if (idx == M - 1) ranges[cur].y = M;
+  }
+}
+
+}  // namespace gs

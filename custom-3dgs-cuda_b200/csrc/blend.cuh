@@ -1,0 +1,346 @@
+// Front-to-back alpha blending of 16x16 tiles and its backward.
+//
+// One CTA of 256 threads per tile, one pixel per thread; warp w covers the 8x4 pixel block
+// at ((w & 1) * 8, (w >> 1) * 4) of the tile, so small splats touch few warps. The tile's
+// depth-sorted Gaussians are consumed in batches of 256 blend records (48 bytes each)
+// gathered with cp.async into a double-buffered shared-memory ring: batch b + 1 is in
+// flight while batch b is blended.
+#pragma once
+
+#include "gs_common.cuh"
+
+namespace gs {
+
+constexpr int kBlendThreads = 256;
+constexpr int kBlendBatch = 256;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void tile_pixel(int tile_x, int tile_y, int& px, int& py) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  px = tile_x * kTileSide + (warp & 1) * 8 + (lane & 7);
+  py = tile_y * kTileSide + (warp >> 1) * 4 + (lane >> 3);
+}
+
+struct BlendFwdParams {
+  int W, H, tiles_x;
+  const int2* ranges;
+  const int* sorted_ids;
+  const float4* records;
+  const int* pair_count;
+  long long pair_capacity;
+  float* img;
+  float* final_T;
+  int* n_contrib;
+};
+
+// Forward blend (csrc/forward/rasterize.cu:188-280): for each pixel, in depth order,
+// alpha = min(0.99, o * exp(power)), skipped when power > 0 or alpha < 1/255; colour
+// accumulates c * alpha * T and T *= 1 - alpha; the pixel stops after the Gaussian that
+// takes T below 1e-4. n_contrib counts Gaussians walked up to the last one applied.
+__global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(BlendFwdParams p) {
+  __shared__ float4 s_rec[2][3][kBlendBatch];
+  if ((long long)(*p.pair_count) > p.pair_capacity) return;
+  const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
+  const int tid = threadIdx.x;
+  int px, py;
+  tile_pixel(tile_x, tile_y, px, py);
+  const bool inside = px < p.W && py < p.H;
+  const int2 range = p.ranges[blockIdx.x];
+  const int K = range.y - range.x;
+  const int nbatches = (K + kBlendBatch - 1) / kBlendBatch;
+
+  auto issue = [&](int b) {
+    const int j = b * kBlendBatch + tid;
+    if (j < K) {
+      const int g = p.sorted_ids[range.x + j];
+      const float4* src = p.records + 3 * (size_t)g;
+      float4(*dst)[kBlendBatch] = s_rec[b & 1];
+      cp_async16(&dst[0][tid], src);
+      cp_async16(&dst[1][tid], src + 1);
+      cp_async16(&dst[2][tid], src + 2);
+    }
+    cp_async_commit();
+  };
+
+  float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
+  int contributor = 0, last = 0;
+  bool done = !inside;
+  const float fpx = (float)px, fpy = (float)py;
+  if (nbatches > 0) issue(0);
+  for (int b = 0; b < nbatches; ++b) {
+    if (b + 1 < nbatches) {
+      issue(b + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int n = min(kBlendBatch, K - b * kBlendBatch);
+    const float4(*rec)[kBlendBatch] = s_rec[b & 1];
+    if (!done) {
+      for (int i = 0; i < n; ++i) {
+        ++contributor;
+        const float4 r0 = rec[0][i];
+        const float4 r1 = rec[1][i];
+        const float dx = fpx - r0.x, dy = fpy - r0.y;
+        const float power = splat_power(make_float3(r0.z, r0.w, r1.x), dx, dy);
+        if (power > 0.0f) continue;
+        const float alpha = fminf(0.99f, r1.y * __expf(power));
+        if (alpha < (1.0f / 255.0f)) continue;
+        const float weight = alpha * T;
+        cr += r1.z * weight;
+        cg += r1.w * weight;
+        cb += rec[2][i].x * weight;
+        T *= (1.0f - alpha);
+        last = contributor;
+        if (T < 1e-4f) {
+          done = true;
+          break;
+        }
+      }
+    }
+    if (__syncthreads_count(done) == kBlendThreads) break;
+  }
+  cp_async_wait<0>();
+  if (inside) {
+    const int pix = py * p.W + px;
+    p.img[3 * pix + 0] = cr;
+    p.img[3 * pix + 1] = cg;
+    p.img[3 * pix + 2] = cb;
+    p.final_T[pix] = T;
+    p.n_contrib[pix] = last;
+  }
+}
+
+struct BlendBwdParams {
+  int N, W, H, tiles_x;
+  const float* grad_img;
+  const int2* ranges;
+  const int* sorted_ids;
+  const float4* records;  // 3 per Gaussian, indexed by Gaussian id
+  const float* final_T;
+  const int* n_contrib;
+  float* g_mean2d;
+  float* g_cov2d;
+  float* g_colors;
+  float* g_alpha;
+};
+
+// Butterfly reduce-scatter of 9 per-lane values over a warp in 12 shuffles. On return the
+// even lane of each lane pair holding a real value index (0..8) has the warp total of
+// that value in *out and the index in *slot; other lanes get slot = -1.
+__device__ __forceinline__ void warp_reduce9(const float (&v)[9], float* out, int* slot) {
+  const int lane = threadIdx.x & 31;
+  const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1,
+             b1 = (lane >> 1) & 1;
+  float w[6];
+  {
+    const float p[10] = {v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], 0.0f};
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const float keep = b4 ? p[k + 5] : p[k];
+      const float send = b4 ? p[k] : p[k + 5];
+      w[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    w[5] = 0.0f;
+  }
+  float x[4];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const float keep = b3 ? w[k + 3] : w[k];
+    const float send = b3 ? w[k] : w[k + 3];
+    x[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  x[3] = 0.0f;
+  float y[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float keep = b2 ? x[k + 2] : x[k];
+    const float send = b2 ? x[k] : x[k + 2];
+    y[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  float z;
+  {
+    const float keep = b1 ? y[1] : y[0];
+    const float send = b1 ? y[0] : y[1];
+    z = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  z += __shfl_xor_sync(0xffffffffu, z, 1);
+  const int xi = (b2 ? 2 : 0) + (b1 ? 1 : 0);
+  const int wi = (b3 ? 3 : 0) + xi;
+  const int vi = (b4 ? 5 : 0) + wi;
+  *out = z;
+  *slot = ((lane & 1) == 0 && xi < 3 && wi < 5 && vi < 9) ? vi : -1;
+}
+
+constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
+
+// Backward blend (csrc/backward/rasterize_backward.cu:60-235). Each pixel replays its
+// Gaussians back to front from its n_contrib, recovering T before each one as
+// T / max(1 - alpha, 1e-4), and produces dL/d(mean, conic, colour, opacity). The tile
+// walk starts at the batch holding the tile's largest n_contrib instead of the list end.
+// Per Gaussian, the 256 pixel contributions are reduced per warp (warp_reduce9) and added
+// into a per-batch shared slot; after each batch the slot sums are converted from
+// dL/dconic to dL/dSigma2 = -V G V (V the conic, G its symmetric gradient) and added to
+// the global gradients with one atomic per component.
+__global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdParams p) {
+  __shared__ float4 s_rec[2][3][kBlendBatch];
+  __shared__ float s_acc[kBlendBatch * kAccStride];
+  __shared__ int s_max_last;
+  const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
+  const int tid = threadIdx.x;
+  int px, py;
+  tile_pixel(tile_x, tile_y, px, py);
+  const bool inside = px < p.W && py < p.H;
+  const int pix = py * p.W + px;
+  const int2 range = p.ranges[blockIdx.x];
+  const int K = range.y - range.x;
+
+  float gr = 0.0f, gg = 0.0f, gb = 0.0f, T = 0.0f;
+  int last = 0;
+  if (inside) {
+    gr = p.grad_img[3 * pix];
+    gg = p.grad_img[3 * pix + 1];
+    gb = p.grad_img[3 * pix + 2];
+    T = p.final_T[pix];
+    last = min(p.n_contrib[pix], K);
+  }
+  if (tid == 0) s_max_last = 0;
+  for (int k = tid; k < kBlendBatch * kAccStride; k += kBlendThreads) s_acc[k] = 0.0f;
+  __syncthreads();
+  const int wmax = __reduce_max_sync(0xffffffffu, last);
+  if ((tid & 31) == 0 && wmax > 0) atomicMax(&s_max_last, wmax);
+  __syncthreads();
+  const int K_eff = s_max_last;  // list prefix that any pixel of this tile replays
+  const int nbatches = (K_eff + kBlendBatch - 1) / kBlendBatch;
+
+  // batch b covers list indices [lo(b), hi(b)) walking from the back
+  auto batch_hi = [&](int b) { return K_eff - b * kBlendBatch; };
+  auto batch_lo = [&](int b) { return max(0, K_eff - (b + 1) * kBlendBatch); };
+  auto issue = [&](int b) {
+    const int lo = batch_lo(b), hi = batch_hi(b);
+    const int j = lo + tid;
+    if (j < hi) {
+      int g = p.sorted_ids[range.x + j];
+      float4(*dst)[kBlendBatch] = s_rec[b & 1];
+      if (g >= 0 && g < p.N) {
+        const float4* src = p.records + 3 * (size_t)g;
+        cp_async16(&dst[0][tid], src);
+        cp_async16(&dst[1][tid], src + 1);
+        cp_async16(&dst[2][tid], src + 2);
+      } else {
+        // out-of-range id: a record that never passes the opacity test and is not flushed
+        dst[0][tid] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        dst[1][tid] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        dst[2][tid] = make_float4(0.0f, __int_as_float(-1), 0.0f, 0.0f);
+      }
+    }
+    cp_async_commit();
+  };
+
+  float ar = 0.0f, ag = 0.0f, ab = 0.0f;  // colour of everything behind, front-weighted
+  const float fpx = (float)px, fpy = (float)py;
+  if (nbatches > 0) issue(0);
+  for (int b = 0; b < nbatches; ++b) {
+    if (b + 1 < nbatches) {
+      issue(b + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int lo = batch_lo(b), hi = batch_hi(b);
+    const float4(*rec)[kBlendBatch] = s_rec[b & 1];
+    for (int j = hi - 1; j >= lo; --j) {
+      const int k = j - lo;  // slot in this batch
+      float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      bool active = false;
+      if (j < last) {  // contributor j + 1 <= n_contrib
+        const float4 r0 = rec[0][k];
+        const float4 r1 = rec[1][k];
+        const float dx = fpx - r0.x, dy = fpy - r0.y;
+        const float cx = r0.z, cy = r0.w, cz = r1.x;
+        const float power = splat_power(make_float3(cx, cy, cz), dx, dy);
+        if (power <= 0.0f) {
+          const float G = __expf(power);
+          const float alpha_raw = r1.y * G;
+          const float alpha = fminf(0.99f, alpha_raw);
+          if (alpha >= (1.0f / 255.0f)) {
+            active = true;
+            const float one_minus = 1.0f - alpha;
+            const float T_before = T / fmaxf(one_minus, 1e-4f);
+            const float c0 = r1.z, c1 = r1.w, c2 = rec[2][k].x;
+            const float wgt = alpha * T_before;
+            v[5] = wgt * gr;
+            v[6] = wgt * gg;
+            v[7] = wgt * gb;
+            const float dL_dalpha =
+                ((c0 - ar) * gr + (c1 - ag) * gg + (c2 - ab) * gb) * T_before;
+            float dL_dpower = 0.0f;
+            if (alpha_raw < 0.99f) {
+              v[8] = G * dL_dalpha;
+              dL_dpower = alpha * dL_dalpha;
+            }
+            v[0] = dL_dpower * (cx * dx + cy * dy);
+            v[1] = dL_dpower * (cy * dx + cz * dy);
+            v[2] = -0.5f * dL_dpower * dx * dx;
+            v[3] = -dL_dpower * dx * dy;
+            v[4] = -0.5f * dL_dpower * dy * dy;
+            ar = alpha * c0 + one_minus * ar;
+            ag = alpha * c1 + one_minus * ag;
+            ab = alpha * c2 + one_minus * ab;
+            T = T_before;
+          }
+        }
+      }
+      if (__any_sync(0xffffffffu, active)) {
+        float sum;
+        int slot;
+        warp_reduce9(v, &sum, &slot);
+        if (slot >= 0 && sum != 0.0f) atomicAdd(&s_acc[k * kAccStride + slot], sum);
+      }
+    }
+    __syncthreads();
+    // flush this batch's slot sums to the global gradients
+    if (tid < hi - lo) {
+      float* acc = &s_acc[tid * kAccStride];
+      const int g = __float_as_int(rec[2][tid].y);
+      bool any = false;
+#pragma unroll
+      for (int q = 0; q < 9; ++q) any |= acc[q] != 0.0f;
+      if (any && g >= 0 && g < p.N) {
+        atomicAdd(p.g_mean2d + 2 * g, acc[0]);
+        atomicAdd(p.g_mean2d + 2 * g + 1, acc[1]);
+        const float vx = rec[0][tid].z, vy = rec[0][tid].w, vz = rec[1][tid].x;
+        const float gx = acc[2], gy = 0.5f * acc[3], gz = acc[4];
+        atomicAdd(p.g_cov2d + 3 * g,
+                  -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz));
+        atomicAdd(p.g_cov2d + 3 * g + 1,
+                  -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz));
+        atomicAdd(p.g_cov2d + 3 * g + 2,
+                  -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz));
+        atomicAdd(p.g_colors + 3 * g, acc[5]);
+        atomicAdd(p.g_colors + 3 * g + 1, acc[6]);
+        atomicAdd(p.g_colors + 3 * g + 2, acc[7]);
+        atomicAdd(p.g_alpha + g, acc[8]);
+      }
+#pragma unroll
+      for (int q = 0; q < kAccStride; ++q) acc[q] = 0.0f;
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+}
+
+}  // namespace gs

@@ -1,0 +1,203 @@
+// Shared device helpers for the sm_100a Gaussian-splatting kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gs {
+
+constexpr int kTileSide = 16;                     // 16 x 16 pixel tiles
+constexpr int kTilePixels = kTileSide * kTileSide;
+
+// Device error bits (OR-ed into g_device_errors by the kernels).
+constexpr unsigned kErrLookbackTimeout = 1u;  // a decoupled look-back wait hit its limit
+constexpr unsigned kErrCapacity = 2u;         // pair count exceeded the pair capacity
+constexpr unsigned kErrBadIndex = 4u;         // an index was out of range
+
+// Iteration limit of every spin-wait. Each iteration is one L2 round trip plus a short
+// sleep, so the limit bounds a wait to well under a second.
+constexpr unsigned kSpinLimit = 1u << 20;
+
+// Real spherical-harmonic normalisation constants for degrees 0..3 (the Inria 3DGS basis;
+// the reference lists them at csrc/forward/SH.cu:12-28).
+constexpr float kShC0 = 0.28209479177387814f;
+constexpr float kShC1 = 0.4886025119029199f;
+constexpr float kShC2_0 = 1.0925484305920792f;
+constexpr float kShC2_1 = -1.0925484305920792f;
+constexpr float kShC2_2 = 0.31539156525252005f;
+constexpr float kShC2_3 = -1.0925484305920792f;
+constexpr float kShC2_4 = 0.5462742152960396f;
+constexpr float kShC3_0 = -0.5900435899266435f;
+constexpr float kShC3_1 = 2.890611442640554f;
+constexpr float kShC3_2 = -0.4570457994644658f;
+constexpr float kShC3_3 = 0.3731763325901154f;
+constexpr float kShC3_4 = -0.4570457994644658f;
+constexpr float kShC3_5 = 1.445305721320277f;
+constexpr float kShC3_6 = -0.5900435899266435f;
+
+extern __device__ unsigned g_device_errors;
+
+__device__ __forceinline__ void raise_device_error(unsigned bits) {
+  atomicOr(&g_device_errors, bits);
+}
+
+// ---------------------------------------------------------------------------------------
+// Tile footprint of one splat. The arithmetic follows the reference's count_overlaps /
+// key_generation (csrc/forward/rasterize.cu:27-57): a 3-sigma radius from the larger
+// eigenvalue of the 2x2 covariance, a pixel bounding box clamped to the image, and the
+// 16x16 tile rectangle [x0,x1) x [y0,y1). The expressions are written as the reference
+// writes them so that nvcc contracts them into the same fused multiply-adds.
+// ---------------------------------------------------------------------------------------
+struct TileRect {
+  int x0, y0, x1, y1;
+};
+
+__device__ __forceinline__ bool splat_tile_rect(float2 mean, float a, float b, float c,
+                                                int width, int height, int tiles_x,
+                                                int tiles_y, TileRect& r) {
+  float det = a * c - b * b;
+  if (det <= 0.0f) return false;
+  float mid = 0.5f * (a + c);
+  float lambda_max = mid + sqrtf(fmaxf(0.1f, mid * mid - det));
+  float radius = ceilf(3.0f * sqrtf(lambda_max));
+  int min_x = max(0, (int)floorf(mean.x - radius));
+  int max_x = min(width, (int)ceilf(mean.x + radius));
+  int min_y = max(0, (int)floorf(mean.y - radius));
+  int max_y = min(height, (int)ceilf(mean.y + radius));
+  int tx0 = min_x / kTileSide, tx1 = (max_x + kTileSide - 1) / kTileSide;
+  int ty0 = min_y / kTileSide, ty1 = (max_y + kTileSide - 1) / kTileSide;
+  r.x0 = max(0, min(tiles_x, tx0));
+  r.x1 = max(0, min(tiles_x, tx1));
+  r.y0 = max(0, min(tiles_y, ty0));
+  r.y1 = max(0, min(tiles_y, ty1));
+  return true;
+}
+
+__device__ __forceinline__ int rect_count(const TileRect& r) {
+  return max(0, r.x1 - r.x0) * max(0, r.y1 - r.y0);
+}
+
+// Conic (inverse 2D covariance) with the reference's guard det <= 0 -> 0
+// (csrc/forward/rasterize.cu:224-232).
+__device__ __forceinline__ float3 conic_from_cov(float a, float b, float c) {
+  float det = a * c - b * b;
+  float det_inv = (det > 0.0f) ? (1.0f / det) : 0.0f;
+  return make_float3(c * det_inv, -b * det_inv, a * det_inv);
+}
+
+// Gaussian falloff exponent of a pixel offset (dx, dy) under a conic; the same expression
+// as csrc/forward/rasterize.cu:249-251.
+__device__ __forceinline__ float splat_power(float3 conic, float dx, float dy) {
+  return -0.5f * (conic.x * dx * dx + 2.0f * conic.y * dx * dy + conic.z * dy * dy);
+}
+
+// ---------------------------------------------------------------------------------------
+// Decoupled look-back status words: bits [31:30] = flag, bits [29:0] = value.
+// ---------------------------------------------------------------------------------------
+constexpr unsigned kFlagAggregate = 1u << 30;
+constexpr unsigned kFlagPrefix = 2u << 30;
+constexpr unsigned kFlagMask = 3u << 30;
+constexpr unsigned kValueMask = (1u << 30) - 1u;
+
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits (bounded) until the status word is published; returns the word, or kFlagPrefix|0
+// after raising kErrLookbackTimeout.
+__device__ __forceinline__ unsigned wait_status(const unsigned* p) {
+  unsigned v = ld_relaxed(p);
+  unsigned spins = 0;
+  while ((v & kFlagMask) == 0u) {
+    if (++spins > kSpinLimit) {
+      raise_device_error(kErrLookbackTimeout);
+      return kFlagPrefix;
+    }
+    __nanosleep(64);
+    v = ld_relaxed(p);
+  }
+  return v;
+}
+
+// Single-thread look-back: exclusive prefix of `tile` from the status words of its
+// predecessors (status[0..tile-1]); each status word is strided by `stride` words.
+__device__ __forceinline__ unsigned lookback_serial(const unsigned* status, int tile,
+                                                    int stride) {
+  unsigned excl = 0;
+  for (int p = tile - 1; p >= 0; --p) {
+    unsigned v = wait_status(status + (size_t)p * stride);
+    excl += v & kValueMask;
+    if (v & kFlagPrefix) break;
+  }
+  return excl;
+}
+
+// Warp-cooperative look-back for a single counter per tile (status stride 1). All 32 lanes
+// call it; every lane returns the exclusive prefix.
+__device__ __forceinline__ unsigned lookback_warp(const unsigned* status, int tile) {
+  const int lane = threadIdx.x & 31;
+  unsigned excl = 0;
+  int base = tile - 1;
+  while (base >= 0) {
+    int p = base - lane;
+    unsigned v = kFlagPrefix;  // lanes past tile 0 act as a zero prefix
+    if (p >= 0) v = wait_status(status + p);
+    unsigned prefix_mask = __ballot_sync(0xffffffffu, (v & kFlagPrefix) != 0u);
+    // lanes up to and including the first (nearest) prefix contribute
+    int stop = prefix_mask ? (__ffs(prefix_mask) - 1) : 31;
+    unsigned contrib = (lane <= stop && p >= 0) ? (v & kValueMask) : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+    excl += contrib;
+    if (prefix_mask) break;
+    base -= 32;
+  }
+  return excl;
+}
+
+// Block-wide exclusive scan of one unsigned per thread (blockDim.x a multiple of 32,
+// <= 1024). `smem` holds at least 33 words. Returns the exclusive prefix; *total gets the
+// block sum.
+__device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* smem,
+                                                         unsigned* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  unsigned incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) smem[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    unsigned w = lane < nwarps ? smem[lane] : 0u;
+    unsigned wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      unsigned n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    if (lane < nwarps) smem[lane] = wi - w;  // exclusive per warp
+    if (lane == nwarps - 1) smem[32] = wi;   // block total
+  }
+  __syncthreads();
+  unsigned excl = smem[warp] + incl - v;
+  *total = smem[32];
+  __syncthreads();
+  return excl;
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+}  // namespace gs

@@ -1,0 +1,97 @@
+"""ctypes binding of libgs3d_b200.so, the C ABI declared in include/gs3d_b200.h.
+
+The library is loaded from this package directory. Loading never falls back to anything:
+if the shared library is missing or lacks a symbol, importing the package raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_longlong, c_size_t, c_uint, c_void_p, POINTER
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libgs3d_b200.so"
+
+GS_OK = 0
+GS_ERR_INVALID_ARG = 1
+GS_ERR_CUDA = 2
+GS_ERR_CAPACITY = 3
+GS_ERR_DEVICE = 4
+
+P = c_void_p  # every pointer crosses the boundary as an integer address
+
+# name -> (restype, argtypes), one entry per declaration in include/gs3d_b200.h
+SIGNATURES = {
+    "gs_last_error": (ctypes.c_char_p, []),
+    "gs_version": (ctypes.c_char_p, []),
+    "gs_project": (c_int, [c_int, P, P, P, P, P, c_float, c_float, c_float, c_float, P, P, P,
+                           P]),
+    "gs_sh_forward": (c_int, [c_int, P, P, P, P, P, P]),
+    "gs_rasterize_workspace_size": (c_size_t, [c_int, c_int, c_int, c_longlong]),
+    "gs_rasterize": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, c_size_t, c_longlong, P,
+                             P, P, P, P, P, P, P, P]),
+    "gs_rasterize_backward_workspace_size": (c_size_t, [c_int]),
+    "gs_rasterize_backward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P,
+                                      c_size_t, P, P, P, P, P]),
+    "gs_sh_backward": (c_int, [c_int, P, P, P, P, P, P, P, P, P]),
+    "gs_project_backward": (c_int, [c_int, P, P, P, P, P, P, P, c_float, c_float, c_float,
+                                    c_float, P, P, P, P]),
+    "gs_event_create": (c_int, [POINTER(c_void_p)]),
+    "gs_event_synchronize": (c_int, [P]),
+    "gs_event_destroy": (c_int, [P]),
+    "gs_device_error_bits": (c_int, [POINTER(c_uint)]),
+    "gs_clear_device_errors": (c_int, []),
+}
+
+
+def load(path: Path = LIB_PATH) -> ctypes.CDLL:
+    if not path.exists():
+        raise ImportError(
+            f"{path.name} is not built; run `python custom-3dgs-cuda_b200/build.py` "
+            "(or __graft_entry__.build()) first"
+        )
+    lib = ctypes.CDLL(str(path))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)  # AttributeError if the symbol is missing
+        fn.restype = restype
+        fn.argtypes = argtypes
+    return lib
+
+
+lib = load()
+
+
+def check(status: int) -> None:
+    """Raises RuntimeError with the library's message when a call did not return GS_OK."""
+    if status != GS_OK:
+        msg = lib.gs_last_error().decode(errors="replace")
+        raise RuntimeError(f"gs3d_b200 error {status}: {msg}")
+
+
+def device_error_bits() -> int:
+    bits = c_uint(0)
+    check(lib.gs_device_error_bits(ctypes.byref(bits)))
+    return int(bits.value)
+
+
+def clear_device_errors() -> None:
+    check(lib.gs_clear_device_errors())
+
+
+class Event:
+    """A CUDA event owned by the library (timing disabled)."""
+
+    def __init__(self) -> None:
+        h = c_void_p(0)
+        check(lib.gs_event_create(ctypes.byref(h)))
+        self.handle = h.value
+
+    def synchronize(self) -> None:
+        check(lib.gs_event_synchronize(self.handle))
+
+    def __del__(self) -> None:
+        try:
+            if self.handle:
+                lib.gs_event_destroy(self.handle)
+        except Exception:
+            pass

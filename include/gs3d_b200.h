@@ -1,0 +1,143 @@
+/*
+ * gs3d_b200.h — C ABI of the B200 (sm_100a) 3D Gaussian Splatting rasterizer.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream handle
+ * (cudaStream_t passed as void*; NULL means the legacy default stream) and returns an
+ * int status (GS_OK or a GS_ERR_* code). On failure gs_last_error() returns a message
+ * for the calling thread. No entry point allocates device memory except where stated;
+ * scratch memory ("workspace") is supplied by the caller and sized by the *_workspace_size
+ * queries. All work is enqueued asynchronously on `stream`.
+ *
+ * Tensor layouts are those of the reference pybind11 module `custom_rasterizer_cuda`
+ * (csrc/bindings.cpp:141-151): row-major fp32, int32 for ids / ranges / counts.
+ *   mu[N,3]  q[N,4] (w,x,y,z)  s[N,3] (log-scale)  R[3,3] (world->camera, row-major)  t[3]
+ *   mean2d[N,2]  cov2d[N,3] = (a,b,c) of [[a,b],[b,c]]  depths[N]  colors[N,3]
+ *   albedo[N,3] (SH DC)  k_j[N,15,3] (SH degrees 1..3, coefficient-major then RGB)
+ *   img[H,W,3]  final_T[H,W]  n_contrib[H,W]  tile_ranges[T,2]  with T = ceil(W/16)*ceil(H/16)
+ */
+#ifndef GS3D_B200_H
+#define GS3D_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define GS_API __attribute__((visibility("default")))
+#else
+#define GS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GS_OK 0
+#define GS_ERR_INVALID_ARG 1   /* bad size, null pointer or misaligned buffer */
+#define GS_ERR_CUDA 2          /* a CUDA runtime call or launch failed */
+#define GS_ERR_CAPACITY 3      /* pair count M exceeded the caller's capacity */
+#define GS_ERR_DEVICE 4        /* a device-side check failed (see gs_device_error_bits) */
+
+/* Message describing the last error raised on the calling thread ("" if none). */
+GS_API const char* gs_last_error(void);
+/* Library version string. */
+GS_API const char* gs_version(void);
+
+/*
+ * Projection forward. Replaces `project` (csrc/bindings.cpp:12-29, kernel
+ * csrc/forward/projection.cu:12-107). Gaussians with camera-space z <= 0.2 get zeros in
+ * all three outputs, as the reference's zero-initialised outputs do.
+ */
+GS_API int gs_project(int N, const float* mu, const float* q, const float* s, const float* R,
+               const float* t, float fx, float fy, float cx, float cy, float* mean2d,
+               float* cov2d, float* depths, void* stream);
+
+/*
+ * Spherical-harmonic colour forward, degrees 0..3. Replaces `SH`
+ * (csrc/bindings.cpp:32-46, kernel csrc/forward/SH.cu:57-93). `cam_pos` is a DEVICE
+ * pointer to 3 floats; unlike the reference no host copy of it is made.
+ */
+GS_API int gs_sh_forward(int N, const float* cam_pos, const float* mu, const float* albedo,
+                  const float* k_j, float* colors, void* stream);
+
+/*
+ * Bytes of caller-provided workspace gs_rasterize needs for N Gaussians, an H x W image
+ * and room for `pair_capacity` (tile, Gaussian) pairs.
+ */
+GS_API size_t gs_rasterize_workspace_size(int N, int H, int W, long long pair_capacity);
+
+/*
+ * Tile binning, depth/tile sort, tile ranges and the front-to-back alpha blend.
+ * Replaces `rasterize` (csrc/bindings.cpp:50-70, host csrc/forward/rasterize.cu:284-486).
+ * Outputs: img[H,W,3], sorted_ids[pair_capacity] (the first M are valid), tile_ranges[T,2]
+ * (empty tiles (0,0)), final_T[H,W], n_contrib[H,W].
+ * The pair count M is written to *pair_count_dev (a device int inside or outside the
+ * workspace) and, when pair_count_host is non-NULL (pinned host memory), copied there
+ * asynchronously; when `m_ready_event` (a cudaEvent_t) is non-NULL it is recorded right
+ * after that copy, so a caller can learn M long before the blend finishes.
+ * If M > pair_capacity every pair-dependent kernel does nothing and the caller must call
+ * again with pair_capacity >= M (the status is still GS_OK: the overflow is only known
+ * on the device). N == 0 or M == 0 produce zero images, final_T = 1, n_contrib = 0 and
+ * zero ranges, as the reference does (rasterize.cu:306-319).
+ */
+GS_API int gs_rasterize(int N, int H, int W, const float* depths, const float* mean2d,
+                 const float* cov2d, const float* colors, const float* alpha, void* workspace,
+                 size_t workspace_bytes, long long pair_capacity, float* img, int* sorted_ids,
+                 int* tile_ranges, float* final_T, int* n_contrib, int* pair_count_dev,
+                 int* pair_count_host, void* m_ready_event, void* stream);
+
+/* Bytes of workspace gs_rasterize_backward needs for N Gaussians. */
+GS_API size_t gs_rasterize_backward_workspace_size(int N);
+
+/*
+ * Backward of the alpha blend. Replaces `backwards_rasterization`
+ * (csrc/bindings.cpp:72-100, kernel csrc/backward/rasterize_backward.cu:6-236).
+ * Gradient outputs are ACCUMULATED (atomic adds) and must be zeroed by the caller:
+ * g_mean2d[N,2], g_cov2d[N,3] (dL/dSigma2, not dL/dconic), g_colors[N,3], g_alpha[N].
+ * `sorted_ids` holds the tile-sorted Gaussian ids addressed by tile_ranges; out-of-range
+ * ids are skipped, as in the reference.
+ */
+GS_API int gs_rasterize_backward(int N, int H, int W, const float* grad_img, const float* mean2d,
+                          const float* cov2d, const float* colors, const float* alpha,
+                          const int* sorted_ids, const int* tile_ranges, const float* final_T,
+                          const int* n_contrib, void* workspace, size_t workspace_bytes,
+                          float* g_mean2d, float* g_cov2d, float* g_colors, float* g_alpha,
+                          void* stream);
+
+/*
+ * Backward of the SH colour. Replaces `backwards_SH` (csrc/bindings.cpp:102-116, kernel
+ * csrc/backward/delight_backward.cu:107-174). Outputs are overwritten (not accumulated).
+ */
+GS_API int gs_sh_backward(int N, const float* grad_colors, const float* mu, const float* albedo,
+                   const float* k_j, const float* cam_pos, float* g_albedo, float* g_k_j,
+                   float* g_mu, void* stream);
+
+/*
+ * Backward of the projection. Replaces `backwards_projection` (csrc/bindings.cpp:118-139,
+ * kernel csrc/backward/projection_backward.cu:11-140). Outputs are overwritten; culled
+ * Gaussians (z <= 0.2) get zeros.
+ */
+GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2d, const float* mu,
+                        const float* q, const float* s, const float* R, const float* t,
+                        float fx, float fy, float cx, float cy, float* g_mu, float* g_q,
+                        float* g_s, void* stream);
+
+/*
+ * CUDA event helpers for m_ready_event (cudaEvent_t values passed as void*): create an event
+ * with timing disabled, block the calling thread until it completes, destroy it.
+ */
+GS_API int gs_event_create(void** event);
+GS_API int gs_event_synchronize(void* event);
+GS_API int gs_event_destroy(void* event);
+
+/*
+ * Device-side error bits recorded by the kernels of earlier calls on this device since
+ * the last gs_clear_device_errors() (1 = a look-back wait gave up, 2 = pair capacity
+ * exceeded, 4 = an index out of range). Synchronises the device.
+ */
+GS_API int gs_device_error_bits(unsigned* bits);
+GS_API int gs_clear_device_errors(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GS3D_B200_H */
