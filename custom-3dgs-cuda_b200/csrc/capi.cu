@@ -1,4 +1,5 @@
 // Library-wide entry points: error reporting, version and the device error word.
+#include <atomic>
 #include <string>
 
 #include "capi_internal.h"
@@ -9,6 +10,9 @@ namespace gs {
 __device__ unsigned g_device_errors = 0u;
 
 static thread_local std::string t_last_error;
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 int set_error(int code, const std::string& msg) {
   t_last_error = msg;
@@ -20,6 +24,10 @@ void clear_error() { t_last_error.clear(); }
 }  // namespace gs
 
 extern "C" const char* gs_last_error(void) { return gs::t_last_error.c_str(); }
+
+extern "C" unsigned long long gs_kernel_launches(void) {
+  return gs::g_launches.load(std::memory_order_relaxed);
+}
 
 extern "C" const char* gs_version(void) { return "gs3d_b200 0.1.0 (sm_100a)"; }
 

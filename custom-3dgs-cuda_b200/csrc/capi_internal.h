@@ -10,6 +10,9 @@
 
 namespace gs {
 
+// Counts kernel launches made by this library (read by gs_kernel_launches).
+void count_launches(unsigned n);
+
 // Records `msg` as the calling thread's last error and returns `code`.
 int set_error(int code, const std::string& msg);
 void clear_error();
@@ -42,4 +45,8 @@ void clear_error();
                                             ") at " __FILE__);                        \
   } while (0)
 
-#define GS_CHECK_LAUNCH() GS_CUDA(cudaGetLastError())
+#define GS_CHECK_LAUNCH()       \
+  do {                          \
+    gs::count_launches(1u);     \
+    GS_CUDA(cudaGetLastError()); \
+  } while (0)

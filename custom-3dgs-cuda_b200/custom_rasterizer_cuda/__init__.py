@@ -23,7 +23,7 @@ import threading
 import torch
 
 from . import _lib
-from ._lib import Event, check, clear_device_errors, device_error_bits, lib
+from ._lib import Event, check, clear_device_errors, device_error_bits, kernel_launches, lib
 
 __all__ = [
     "project",
@@ -34,6 +34,7 @@ __all__ = [
     "backwards_projection",
     "device_error_bits",
     "clear_device_errors",
+    "kernel_launches",
 ]
 
 TILE = 16

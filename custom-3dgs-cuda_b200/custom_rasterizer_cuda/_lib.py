@@ -39,6 +39,7 @@ SIGNATURES = {
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),
+    "gs_kernel_launches": (ctypes.c_ulonglong, []),
     "gs_device_error_bits": (c_int, [POINTER(c_uint)]),
     "gs_clear_device_errors": (c_int, []),
 }
@@ -72,6 +73,11 @@ def device_error_bits() -> int:
     bits = c_uint(0)
     check(lib.gs_device_error_bits(ctypes.byref(bits)))
     return int(bits.value)
+
+
+def kernel_launches() -> int:
+    """Kernels launched by libgs3d_b200 in this process so far."""
+    return int(lib.gs_kernel_launches())
 
 
 def clear_device_errors() -> None:

@@ -1,0 +1,169 @@
+"""View-parallel training step (the benchmark's config 4).
+
+A batch of B camera views is split across the ranks of a process group (rank r renders views
+r, r + world, ...). Every rank holds the full Gaussian set and the Adam state. Per step each
+rank renders its views with the drop-in rasterizer, backpropagates
+0.8 * L1 + 0.2 * (1 - SSIM) per view, and accumulates parameter gradients into ONE flat fp32
+bucket (the parameters' .grad tensors are views into it). One all-reduce (SUM) of the bucket
+and a divide by B then give every rank the batch-mean gradient, and Adam runs on every rank
+identically. The densification statistics of the reference trainer
+(gaussian_splatting/utils/adc.py:58-87: the per-Gaussian sum and count of the screen-space
+mean-gradient norm scaled by (W/2, H/2)) are SUM-reduced with the bucket; the per-Gaussian
+maximum of that norm over the batch is MAX-reduced separately.
+
+With world size 1 no collective runs. Collectives go through torch.distributed (NCCL on GPUs,
+gloo in the CPU tests).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+PARAM_NAMES = ("mu", "q", "s", "alpha", "A", "k_j")
+# Adam learning rates of config 4 (means, quaternions, log-scales, opacity, SH DC, SH rest)
+LEARNING_RATES = {"mu": 1.6e-4, "q": 1e-3, "s": 5e-3, "alpha": 5e-2, "A": 2.5e-3, "k_j": 2.5e-3}
+LAMBDA_DSSIM = 0.2
+
+
+def gaussian_window(size: int = 11, sigma: float = 1.5, device=None) -> torch.Tensor:
+    x = torch.arange(size, dtype=torch.float32, device=device) - (size - 1) / 2.0
+    g = torch.exp(-(x * x) / (2.0 * sigma * sigma))
+    g = g / g.sum()
+    return torch.outer(g, g)
+
+
+def ssim(img: torch.Tensor, ref: torch.Tensor, window: torch.Tensor) -> torch.Tensor:
+    """Mean SSIM of two [H, W, 3] images in [0, 1] with an 11x11 Gaussian window
+    (sigma 1.5), zero padding, C1 = 0.01^2, C2 = 0.03^2."""
+    x = img.permute(2, 0, 1).unsqueeze(0)
+    y = ref.permute(2, 0, 1).unsqueeze(0)
+    C = x.shape[1]
+    w = window.expand(C, 1, *window.shape).contiguous()
+    pad = window.shape[-1] // 2
+    mu_x = F.conv2d(x, w, padding=pad, groups=C)
+    mu_y = F.conv2d(y, w, padding=pad, groups=C)
+    sxx = F.conv2d(x * x, w, padding=pad, groups=C) - mu_x * mu_x
+    syy = F.conv2d(y * y, w, padding=pad, groups=C) - mu_y * mu_y
+    sxy = F.conv2d(x * y, w, padding=pad, groups=C) - mu_x * mu_y
+    c1, c2 = 0.01 ** 2, 0.03 ** 2
+    num = (2 * mu_x * mu_y + c1) * (2 * sxy + c2)
+    den = (mu_x * mu_x + mu_y * mu_y + c1) * (sxx + syy + c2)
+    return (num / den).mean()
+
+
+def reconstruction_loss(img: torch.Tensor, target: torch.Tensor, window: torch.Tensor) -> torch.Tensor:
+    l1 = (img - target).abs().mean()
+    return (1.0 - LAMBDA_DSSIM) * l1 + LAMBDA_DSSIM * (1.0 - ssim(img, target, window))
+
+
+@dataclass
+class ShardPlan:
+    """Which views of a batch of `batch` a rank renders."""
+
+    rank: int
+    world: int
+    batch: int
+
+    def views(self) -> list[int]:
+        return list(range(self.rank, self.batch, self.world))
+
+
+class FlatGrads:
+    """One contiguous fp32 buffer backing the .grad of every parameter, followed by the
+    densification sums (per Gaussian: norm sum, count)."""
+
+    def __init__(self, params: list[torch.Tensor], n_gaussians: int):
+        sizes = [p.numel() for p in params]
+        self.n_param = sum(sizes)
+        self.n = n_gaussians
+        dev = params[0].device
+        self.buffer = torch.zeros(self.n_param + 2 * n_gaussians, device=dev, dtype=torch.float32)
+        off = 0
+        self.views = []
+        for p, k in zip(params, sizes):
+            v = self.buffer[off:off + k].view_as(p)
+            p.grad = v
+            self.views.append(v)
+            off += k
+        self.grad_norm_sum = self.buffer[self.n_param:self.n_param + n_gaussians]
+        self.grad_count = self.buffer[self.n_param + n_gaussians:]
+        self.max_grad = torch.zeros(n_gaussians, device=dev, dtype=torch.float32)
+
+    def zero(self) -> None:
+        self.buffer.zero_()
+        self.max_grad.zero_()
+
+    def rebind(self, params: list[torch.Tensor]) -> None:
+        for p, v in zip(params, self.views):
+            p.grad = v
+
+
+def accumulate_view_stats(fg: FlatGrads, mean2d_grad: torch.Tensor, width: int,
+                          height: int) -> None:
+    """adc.py:58-80 statistics for one view: ||dL/dmean2d * (W/2, H/2)|| summed and counted
+    where non-zero, and its running maximum."""
+    scale = torch.tensor([width / 2.0, height / 2.0], device=mean2d_grad.device)
+    norm = (mean2d_grad[:, :2] * scale).norm(dim=-1)
+    visible = norm > 0
+    fg.grad_norm_sum.add_(torch.where(visible, norm, torch.zeros_like(norm)))
+    fg.grad_count.add_(visible.to(norm.dtype))
+    torch.maximum(fg.max_grad, norm, out=fg.max_grad)
+
+
+def reduce_step(fg: FlatGrads, batch: int, world: int, group=None) -> None:
+    """Batch-mean gradients and the densification statistics across ranks."""
+    if world > 1:
+        dist.all_reduce(fg.buffer, op=dist.ReduceOp.SUM, group=group)
+        dist.all_reduce(fg.max_grad, op=dist.ReduceOp.MAX, group=group)
+    fg.buffer[:fg.n_param].div_(float(batch))
+
+
+class Trainer:
+    """Parameters, optimizer and flat gradient bucket of one rank."""
+
+    def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
+                 fused_adam: bool = True):
+        from gaussian_splatting.scene.gaussian import gaussian
+
+        self.device = device
+        self.rank, self.world, self.group = rank, world, group
+        g = gaussian(scene.N)
+        for name, t in zip(PARAM_NAMES, scene.params()):
+            setattr(g, name, torch.nn.Parameter(t.to(device).contiguous()))
+        self.gaussians = g
+        self.params = [getattr(g, n) for n in PARAM_NAMES]
+        self.views = [v.as_dict(device) for v in views]
+        self.targets = targets
+        self.plan = ShardPlan(rank, world, len(views))
+        self.window = gaussian_window(device=device)
+        groups = [{"params": [getattr(g, n)], "lr": LEARNING_RATES[n], "name": n}
+                  for n in PARAM_NAMES]
+        kw = {"fused": True} if (fused_adam and device.type == "cuda") else {}
+        self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15, **kw)
+        self.fg = FlatGrads(self.params, scene.N)
+
+    def step(self, targets=None) -> torch.Tensor:
+        """One training step over this rank's share of the batch; returns the summed loss of
+        the local views (a 0-d tensor on the device)."""
+        from gaussian_splatting.rasterizer.rasterize import RasterizeFunction, rasterize
+
+        targets = self.targets if targets is None else targets
+        self.fg.zero()
+        self.fg.rebind(self.params)
+        total = torch.zeros((), device=self.device)
+        for vi in self.plan.views():
+            view = self.views[vi]
+            img = rasterize(self.gaussians, view)
+            loss = reconstruction_loss(img, targets[vi], self.window)
+            loss.backward()
+            accumulate_view_stats(self.fg, RasterizeFunction.last_mean2d_grad, view["width"],
+                                  view["height"])
+            total = total + loss.detach()
+        reduce_step(self.fg, len(self.views), self.world, self.group)
+        self.opt.step()
+        return total

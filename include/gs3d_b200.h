@@ -128,6 +128,9 @@ GS_API int gs_event_create(void** event);
 GS_API int gs_event_synchronize(void* event);
 GS_API int gs_event_destroy(void* event);
 
+/* Number of kernels this library has launched in this process (all devices, all threads). */
+GS_API unsigned long long gs_kernel_launches(void);
+
 /*
  * Device-side error bits recorded by the kernels of earlier calls on this device since
  * the last gs_clear_device_errors() (1 = a look-back wait gave up, 2 = pair capacity
