@@ -2,6 +2,7 @@
 // histograms and look-back status words) are cleared at the start of every call.
 #pragma once
 
+#include <cuda_runtime.h>
 #include <stddef.h>
 
 namespace gs {
@@ -26,5 +27,13 @@ struct RasterLayout {
 };
 
 RasterLayout make_raster_layout(int N, int W, int H, long long capacity);
+
+// Enqueues binning, sorting and blending with `ws` laid out as `L` (defined in raster.cu).
+int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* depths,
+                     const float* mean2d, const float* cov2d, const float* colors,
+                     const float* alpha, char* ws, long long capacity, float* img,
+                     int* sorted_ids, int* tile_ranges, float* final_T, int* n_contrib,
+                     int* pair_count_dev, int* pair_count_host, cudaEvent_t m_ready,
+                     cudaStream_t stream);
 
 }  // namespace gs

@@ -30,6 +30,8 @@ SIGNATURES = {
     "gs_rasterize_workspace_size": (c_size_t, [c_int, c_int, c_int, c_longlong]),
     "gs_rasterize": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, c_size_t, c_longlong, P,
                              P, P, P, P, P, P, P, P]),
+    "gs_rasterize_noalloc": (c_int, [c_int, c_int, c_int, P, P, P, P, P, c_longlong, P, P, P,
+                                     P, P, P, P]),
     "gs_rasterize_backward_workspace_size": (c_size_t, [c_int]),
     "gs_rasterize_backward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P,
                                       c_size_t, P, P, P, P, P]),

@@ -84,6 +84,24 @@ GS_API int gs_rasterize(int N, int H, int W, const float* depths, const float* m
                  int* tile_ranges, float* final_T, int* n_contrib, int* pair_count_dev,
                  int* pair_count_host, void* m_ready_event, void* stream);
 
+/*
+ * gs_rasterize without a workspace, for callers that cannot allocate device memory when they
+ * render (a plugin given only its input and output buffers, a process whose device memory is
+ * reserved by another allocator, a per-frame path that must not hit cudaMalloc's device
+ * synchronisation). No counterpart in the reference: it adds an allocation-free way in.
+ * Binning/sort scratch comes from a 16 MiB array compiled into the library (held on every
+ * device that loads it); calls whose layout for (N, H, W, pair_capacity) does not fit return
+ * GS_ERR_CAPACITY before any GPU work. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress), so make it before any stream capture. Calls share the array: GPU
+ * work of overlapping calls races and must be serialised by the caller. Outputs and M (into
+ * *pair_count_dev when non-NULL) as gs_rasterize; nothing is allocated.
+ */
+GS_API int gs_rasterize_noalloc(int N, int H, int W, const float* depths, const float* mean2d,
+                                const float* cov2d, const float* colors, const float* alpha,
+                                long long pair_capacity, float* img, int* sorted_ids,
+                                int* tile_ranges, float* final_T, int* n_contrib,
+                                int* pair_count_dev, void* stream);
+
 /* Bytes of workspace gs_rasterize_backward needs for N Gaussians. */
 GS_API size_t gs_rasterize_backward_workspace_size(int N);
 
