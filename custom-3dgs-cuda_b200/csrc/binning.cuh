@@ -58,42 +58,40 @@ struct BinParams {
   long long pair_capacity;
 };
 
-__global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
-  __shared__ unsigned s_tile, s_prefix;
-  __shared__ unsigned s_scan[33];
-  __shared__ unsigned s_hist[4][256];
-  __shared__ bool s_last;
-  const int tid = threadIdx.x;
-  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
-  for (int i = tid; i < 4 * 256; i += kBinThreads) (&s_hist[0][0])[i] = 0u;
-  __syncthreads();
-  const int tile = (int)s_tile;
-  const int i = tile * kBinThreads + tid;
-
-  unsigned count = 0, depth_bits = 0;
-  if (i < p.N) {
-    const float2 mean = make_float2(__ldg(p.mean2d + 2 * i), __ldg(p.mean2d + 2 * i + 1));
-    const float a = __ldg(p.cov2d + 3 * i), b = __ldg(p.cov2d + 3 * i + 1),
-                c = __ldg(p.cov2d + 3 * i + 2);
-    TileRect r;
-    if (splat_tile_rect(mean, a, b, c, p.W, p.H, p.tiles_x, p.tiles_y, r)) {
-      count = (unsigned)rect_count(r);
-      if (count > 0) {
-        p.rects[i] = pack_rect(r);
-        const float3 conic = conic_from_cov(a, b, c);
-        const float op = __ldg(p.alpha + i);
-        const float cr = __ldg(p.colors + 3 * i), cg = __ldg(p.colors + 3 * i + 1),
-                    cb = __ldg(p.colors + 3 * i + 2);
-        p.records[3 * i + 0] = make_float4(mean.x, mean.y, conic.x, conic.y);
-        p.records[3 * i + 1] = make_float4(conic.z, op, cr, cg);
-        p.records[3 * i + 2] = make_float4(cb, __int_as_float(i), 0.0f, 0.0f);
-        depth_bits = __float_as_uint(__ldg(p.depths + i));
-      }
+// Per-Gaussian part of binning: tile rectangle and count of a projected splat; for a splat
+// covering at least one tile it also writes the packed rectangle and the blend record and
+// returns the depth key. Shared by bin_prepare_kernel and the fused render preprocess.
+__device__ __forceinline__ unsigned bin_gaussian(const BinParams& p, int i, float2 mean,
+                                                 float a, float b, float c, float depth,
+                                                 float3 color, float opacity,
+                                                 unsigned& depth_bits) {
+  TileRect r;
+  unsigned count = 0;
+  depth_bits = 0;
+  if (splat_tile_rect(mean, a, b, c, p.W, p.H, p.tiles_x, p.tiles_y, r)) {
+    count = (unsigned)rect_count(r);
+    if (count > 0) {
+      p.rects[i] = pack_rect(r);
+      const float3 conic = conic_from_cov(a, b, c);
+      p.records[3 * i + 0] = make_float4(mean.x, mean.y, conic.x, conic.y);
+      p.records[3 * i + 1] = make_float4(conic.z, opacity, color.x, color.y);
+      p.records[3 * i + 2] = make_float4(color.z, __int_as_float(i), 0.0f, 0.0f);
+      depth_bits = __float_as_uint(depth);
     }
   }
-  const unsigned visible = count > 0 ? 1u : 0u;
+  return count;
+}
 
-  // order-preserving compaction of visible Gaussians (decoupled look-back over tiles)
+// Block part of binning, called by all kBinThreads threads of a CTA that holds binning tile
+// `tile` (Gaussians [tile * kBinThreads, ...)): order-preserving compaction of the visible
+// Gaussians into the depth-sort input (decoupled look-back), the digit histograms of the four
+// depth passes, the running pair total and, in the last CTA to finish, M and N_visible.
+__device__ __forceinline__ void bin_block(const BinParams& p, int tile, int i, unsigned count,
+                                          unsigned depth_bits, unsigned* s_scan,
+                                          unsigned (*s_hist)[256], unsigned& s_prefix,
+                                          bool& s_last) {
+  const int tid = threadIdx.x;
+  const unsigned visible = count > 0 ? 1u : 0u;
   unsigned n_vis_tile;
   const unsigned excl = block_exclusive_scan(visible, s_scan, &n_vis_tile);
   if (tid == 0)
@@ -138,6 +136,34 @@ __global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
     *p.pair_count = (int)clamped;
     if (m > 0x7fffffffull) raise_device_error(kErrCapacity);
   }
+}
+
+__global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
+  __shared__ unsigned s_tile, s_prefix;
+  __shared__ unsigned s_scan[33];
+  __shared__ unsigned s_hist[4][256];
+  __shared__ bool s_last;
+  const int tid = threadIdx.x;
+  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
+  for (int i = tid; i < 4 * 256; i += kBinThreads) (&s_hist[0][0])[i] = 0u;
+  __syncthreads();
+  const int tile = (int)s_tile;
+  const int i = tile * kBinThreads + tid;
+  unsigned count = 0, depth_bits = 0;
+  if (i < p.N) {
+    const float2 mean = make_float2(__ldg(p.mean2d + 2 * i), __ldg(p.mean2d + 2 * i + 1));
+    const float a = __ldg(p.cov2d + 3 * i), b = __ldg(p.cov2d + 3 * i + 1),
+                c = __ldg(p.cov2d + 3 * i + 2);
+    // colours and opacity are only read for splats that cover a tile
+    TileRect r;
+    if (splat_tile_rect(mean, a, b, c, p.W, p.H, p.tiles_x, p.tiles_y, r) && rect_count(r) > 0) {
+      const float3 col = make_float3(__ldg(p.colors + 3 * i), __ldg(p.colors + 3 * i + 1),
+                                     __ldg(p.colors + 3 * i + 2));
+      count = bin_gaussian(p, i, mean, a, b, c, __ldg(p.depths + i), col, __ldg(p.alpha + i),
+                           depth_bits);
+    }
+  }
+  bin_block(p, tile, i, count, depth_bits, s_scan, s_hist, s_prefix, s_last);
 }
 
 struct DupParams {

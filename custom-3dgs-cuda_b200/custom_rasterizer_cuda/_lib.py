@@ -38,6 +38,9 @@ SIGNATURES = {
     "gs_sh_backward": (c_int, [c_int, P, P, P, P, P, P, P, P, P]),
     "gs_project_backward": (c_int, [c_int, P, P, P, P, P, P, P, c_float, c_float, c_float,
                                     c_float, P, P, P, P]),
+    "gs_l1_ssim_workspace_size": (c_size_t, [c_int, c_int]),
+    "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
+    "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),

@@ -1,0 +1,56 @@
+"""The training step's photometric loss, 0.8 * L1 + 0.2 * (1 - SSIM), as one autograd op over
+the fused kernels of libgs3d_b200 (gs_l1_ssim_forward / gs_l1_ssim_backward).
+
+`l1_ssim_loss(img, target)` matches `train_step.reconstruction_loss` (the torch formulation:
+11x11 Gaussian window, sigma 1.5, zero padding) on [H, W, 3] fp32 CUDA images.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from custom_rasterizer_cuda import _lib
+
+LAMBDA_DSSIM = 0.2
+
+
+class FusedL1SSIM(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, img: torch.Tensor, target: torch.Tensor, lambda_dssim: float = LAMBDA_DSSIM):
+        if not (img.is_cuda and target.is_cuda):
+            raise RuntimeError("l1_ssim_loss needs CUDA tensors")
+        if img.dim() != 3 or img.shape[2] != 3 or img.shape != target.shape:
+            raise RuntimeError("l1_ssim_loss expects two [H, W, 3] images of the same shape")
+        img = img.contiguous().float()
+        target = target.contiguous().float()
+        H, W = int(img.shape[0]), int(img.shape[1])
+        dev = img.device
+        ws_bytes = _lib.lib.gs_l1_ssim_workspace_size(H, W)
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+        loss = torch.empty((), device=dev, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib.gs_l1_ssim_forward(
+                H, W, img.data_ptr(), target.data_ptr(), float(lambda_dssim), ws.data_ptr(),
+                ws_bytes, loss.data_ptr(), None, torch.cuda.current_stream(dev).cuda_stream))
+        ctx.save_for_backward(img, target, ws)
+        ctx.lambda_dssim = float(lambda_dssim)
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad_loss: torch.Tensor):
+        img, target, ws = ctx.saved_tensors
+        H, W = int(img.shape[0]), int(img.shape[1])
+        dev = img.device
+        grad_loss = grad_loss.contiguous().float().reshape(())
+        grad = torch.empty_like(img)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib.gs_l1_ssim_backward(
+                H, W, img.data_ptr(), target.data_ptr(), ctx.lambda_dssim, ws.data_ptr(),
+                ws.numel(), grad_loss.data_ptr(), grad.data_ptr(),
+                torch.cuda.current_stream(dev).cuda_stream))
+        return grad, None, None
+
+
+def l1_ssim_loss(img: torch.Tensor, target: torch.Tensor,
+                 lambda_dssim: float = LAMBDA_DSSIM) -> torch.Tensor:
+    return FusedL1SSIM.apply(img, target, lambda_dssim)

@@ -127,7 +127,7 @@ class Trainer:
     """Parameters, optimizer and flat gradient bucket of one rank."""
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
-                 fused_adam: bool = True):
+                 fused_adam: bool = True, fused_loss: bool = True):
         from gaussian_splatting.scene.gaussian import gaussian
 
         self.device = device
@@ -146,6 +146,7 @@ class Trainer:
         kw = {"fused": True} if (fused_adam and device.type == "cuda") else {}
         self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15, **kw)
         self.fg = FlatGrads(self.params, scene.N)
+        self.fused_loss = fused_loss and device.type == "cuda"
 
     def step(self, targets=None) -> torch.Tensor:
         """One training step over this rank's share of the batch; returns the summed loss of
@@ -159,7 +160,12 @@ class Trainer:
         for vi in self.plan.views():
             view = self.views[vi]
             img = rasterize(self.gaussians, view)
-            loss = reconstruction_loss(img, targets[vi], self.window)
+            if self.fused_loss:
+                from gs3d_b200.loss import l1_ssim_loss
+
+                loss = l1_ssim_loss(img, targets[vi], LAMBDA_DSSIM)
+            else:
+                loss = reconstruction_loss(img, targets[vi], self.window)
             loss.backward()
             accumulate_view_stats(self.fg, RasterizeFunction.last_mean2d_grad, view["width"],
                                   view["height"])

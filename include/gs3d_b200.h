@@ -139,6 +139,23 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
                         float* g_s, void* stream);
 
 /*
+ * Fused photometric loss of the training step (no counterpart in the reference's extension;
+ * the reference trainer computes it with torchmetrics, gaussian_splatting/utils/loss.py:12-33):
+ * loss = (1 - lambda) * mean|img - target| + lambda * (1 - SSIM), SSIM with an 11x11 Gaussian
+ * window (sigma 1.5), zero padding, C1 = 0.01^2, C2 = 0.03^2, over [H, W, 3] images.
+ * The forward writes the scalar loss (and the mean SSIM when ssim_value is non-NULL) to device
+ * memory and leaves per-pixel derivative maps in the workspace for the backward, which writes
+ * grad_img = dL/dimg scaled by *grad_loss (a device scalar).
+ */
+GS_API size_t gs_l1_ssim_workspace_size(int H, int W);
+GS_API int gs_l1_ssim_forward(int H, int W, const float* img, const float* target,
+                              float lambda_dssim, void* workspace, size_t workspace_bytes,
+                              float* loss, float* ssim_value, void* stream);
+GS_API int gs_l1_ssim_backward(int H, int W, const float* img, const float* target,
+                               float lambda_dssim, const void* workspace, size_t workspace_bytes,
+                               const float* grad_loss, float* grad_img, void* stream);
+
+/*
  * CUDA event helpers for m_ready_event (cudaEvent_t values passed as void*): create an event
  * with timing disabled, block the calling thread until it completes, destroy it.
  */
