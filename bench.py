@@ -136,14 +136,47 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
-# ---- per-view breakdown (rank 0) -------------------------------------------------------------
+# ---- per-stage timing ----------------------------------------------------------------------
+STAGES = {  # name: (start mark, end mark) of gs_set_stage_events
+    "preprocess": (0, 1), "depth_sort": (1, 2), "duplicate": (2, 3), "tile_sort": (3, 4),
+    "tile_ranges": (4, 5), "blend_forward": (5, 6), "blend_backward": (7, 8),
+    "gaussian_backward": (8, 9),
+}
+N_MARKS = 10
+
+
+class StageTimer:
+    """One set of timed library events per (step, view); installed before each view renders
+    so every render of the timed region is timed on its own stream."""
+
+    def __init__(self, n_sets: int):
+        from custom_rasterizer_cuda import _lib
+
+        self._lib = _lib
+        self.sets = [[_lib.Event(timed=True) for _ in range(N_MARKS)] for _ in range(n_sets)]
+        self.used = 0
+
+    def install_next(self) -> None:
+        self._lib.set_stage_events(self.sets[self.used])
+        self.used += 1
+
+    def remove(self) -> None:
+        self._lib.set_stage_events(None)
+
+    def stage_ms(self) -> dict:
+        out = {}
+        for name, (a, b) in STAGES.items():
+            vals = [ev[a].elapsed_ms(ev[b]) for ev in self.sets[:self.used]]
+            out[name] = statistics.mean(vals) if vals else None
+        return out
+
+
 def per_view_breakdown(trainer, view: dict, reps: int = 5) -> dict:
-    """Forward / backward ms of one view through the wrapper and per C-ABI call timings."""
-    import custom_rasterizer_cuda as crc
+    """Forward / backward ms of one view through RasterizeFunction (CUDA events around the
+    autograd calls) and its pair statistics."""
     from gaussian_splatting.rasterizer.rasterize import rasterize
 
     g = trainer.gaussians
-    dev = trainer.device
     fwd, bwd = [], []
     for i in range(reps + 2):
         for p in trainer.params:
@@ -152,83 +185,65 @@ def per_view_breakdown(trainer, view: dict, reps: int = 5) -> dict:
         e0.record()
         img = rasterize(g, view)
         e1.record()
-        img.sum().backward()
+        img.backward(torch.ones_like(img))
         e2.record()
         torch.cuda.synchronize()
         if i >= 2:
             fwd.append(e0.elapsed_time(e1))
             bwd.append(e1.elapsed_time(e2))
     trainer.fg.rebind(trainer.params)
+    return {"fwd_ms": statistics.median(fwd), "bwd_ms": statistics.median(bwd),
+            "fps": 1000.0 / statistics.median(fwd)}
 
-    # per C-ABI call (events on the launching stream)
+
+def view_pair_stats(trainer, views: list[dict]) -> dict:
+    """Pairs M and replayed (pixel, Gaussian) pairs (sum of n_contrib) of each view."""
+    from custom_rasterizer_cuda.render import render_forward
+
+    pairs, replayed = [], []
     with torch.no_grad():
         mu, q, s, al, A, kj = (p.detach() for p in trainer.params)
-        R, t = view["R"], view["T"]
-        H, W = view["height"], view["width"]
         op = torch.sigmoid(al).contiguous()
-        cam = (-(R.T @ t)).contiguous()
-        stages = {}
-        times = {k: [] for k in ("project", "SH", "rasterize", "backwards_rasterization",
-                                 "backwards_SH", "backwards_projection")}
-        for i in range(reps + 1):
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
-            ev[0].record()
-            mean2d, cov2d, depths = crc.project(mu.shape[0], mu, q, s, R, t, view["fx"],
-                                                view["fy"], view["cx"], view["cy"])
-            ev[1].record()
-            colors = crc.SH(mu.shape[0], cam, mu, A, kj)
-            ev[2].record()
-            img, ids, ranges, fT, nc = crc.rasterize(mu.shape[0], depths, mean2d, cov2d, colors,
-                                                     op, H, W)
-            ev[3].record()
-            gimg = torch.ones_like(img)
-            ev3b = torch.cuda.Event(enable_timing=True)
-            ev3b.record()
-            gm, gc, gcol, ga = crc.backwards_rasterization(gimg, mean2d, cov2d, colors, op, ids,
-                                                           ranges, fT, nc, mu.shape[0], H, W)
-            ev[4].record()
-            crc.backwards_SH(gcol, mu, A, kj, cam)
-            ev[5].record()
-            crc.backwards_projection(gm, gc, mu, q, s, R, t, view["fx"], view["fy"], view["cx"],
-                                     view["cy"])
-            ev[6].record()
-            torch.cuda.synchronize()
-            if i >= 1:
-                times["project"].append(ev[0].elapsed_time(ev[1]))
-                times["SH"].append(ev[1].elapsed_time(ev[2]))
-                times["rasterize"].append(ev[2].elapsed_time(ev[3]))
-                times["backwards_rasterization"].append(ev3b.elapsed_time(ev[4]))
-                times["backwards_SH"].append(ev[4].elapsed_time(ev[5]))
-                times["backwards_projection"].append(ev[5].elapsed_time(ev[6]))
-        for k, v in times.items():
-            stages[k] = statistics.median(v)
-        M = int(ids.numel())
-        n_contrib_sum = int(nc.sum().item())
-        visible = int((depths > 0).sum().item())
-    return {"fwd_ms": statistics.median(fwd), "bwd_ms": statistics.median(bwd),
-            "fps": 1000.0 / statistics.median(fwd), "stages_ms": stages, "pairs": M,
-            "visible": visible, "replayed_pairs": n_contrib_sum}
+        for v in views:
+            R, t = v["R"], v["T"]
+            cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+            _, _, st = render_forward(mu, q, s, op, A, kj, R, t, cam, v["fx"], v["fy"], v["cx"],
+                                      v["cy"], v["height"], v["width"])
+            pairs.append(st.pairs)
+            replayed.append(int(st.n_contrib.sum().item()))
+    return {"pairs": pairs, "replayed_pairs": replayed}
 
 
-def roofline_entry(bd: dict, pk: dict, n: int) -> dict:
-    """Roofline of the dominant stage of one view. Blend stages are FP32-issue bound (no
-    dense contraction anywhere); the per-Gaussian stages are HBM bound."""
-    st = bd["stages_ms"]
-    name = max(st, key=st.get)
-    ms = st[name]
-    # algorithmic bytes per Gaussian / flops per evaluated (pixel, Gaussian) pair
-    bytes_per_g = {"project": 64, "SH": 216, "backwards_SH": 420, "backwards_projection": 100}
-    if name in bytes_per_g:
-        achieved = bytes_per_g[name] * n / (ms * 1e-3) / 1e9
+def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int) -> dict:
+    """Roofline of the dominant stage over the timed region. The blends are FP32-issue bound
+    (no dense contraction anywhere on the path); the per-Gaussian stages are HBM bound."""
+    name = max((k for k in stage_ms if stage_ms[k] is not None), key=lambda k: stage_ms[k])
+    ms = stage_ms[name]
+    mean_replayed = statistics.mean(stats["replayed_pairs"])
+    mean_pairs = statistics.mean(stats["pairs"])
+    # algorithmic bytes per unit (DESIGN.md section 3)
+    hbm_bytes = {
+        "preprocess": 236 * n + 56 * n,             # parameters in; rects + records out
+        "depth_sort": 4 * 16 * n,                   # 4 passes over (key, id) of N_v <= N
+        "duplicate": 12 * n + 8 * mean_pairs,
+        "tile_sort": 2 * 16 * mean_pairs,
+        "tile_ranges": 8 * mean_pairs,
+        "gaussian_backward": 48 * n + 236 * n + 236 * n + 8 * n,
+    }
+    if name in hbm_bytes:
+        achieved = hbm_bytes[name] / (ms * 1e-3) / 1e9
         return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
-                "peak_source": pk["source"]}
+                "peak_source": pk["source"], "ms_per_launch": ms}
     fp32_peak = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6 / 1e12  # TFLOP/s
-    flops_per_pair = 40.0 if name == "backwards_rasterization" else 14.0
-    achieved = flops_per_pair * bd["replayed_pairs"] / (ms * 1e-3) / 1e12
+    flops_per_pair = 40.0 if name == "blend_backward" else 14.0
+    achieved = flops_per_pair * mean_replayed / (ms * 1e-3) / 1e12
     return {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": fp32_peak,
             "unit": "TFLOP/s", "frac": achieved / fp32_peak, "traffic": None,
-            "peak_source": "derived: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz"}
+            "peak_source": "derived: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz",
+            "ms_per_launch": ms,
+            "unit_of_work": f"{flops_per_pair:.0f} FLOP per replayed (pixel, Gaussian) pair, "
+                            f"{mean_replayed:.3g} per view"}
 
 
 # ---- CPU baseline (the oracle) ----------------------------------------------------------------
@@ -335,6 +350,7 @@ def run_ours(args, rank, world, local) -> int:
 
     # ---- timed region: targets resident in HBM ----
     sampler = ClockSampler(local)
+    timer = StageTimer(args.steps * len(mine))
     barrier(world)
     torch.cuda.synchronize()
     sampler.start()
@@ -342,12 +358,14 @@ def run_ours(args, rank, world, local) -> int:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        trainer.step()
+        trainer.step(before_view=lambda vi: timer.install_next())
     e1.record()
     torch.cuda.synchronize()
     barrier(world)
+    timer.remove()
     launches = crc.kernel_launches() - launches0
     clocks = sampler.stop()
+    stage_ms = timer.stage_ms()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1), world)
     total_launches = int(sum_over_ranks(float(launches), world))
 
@@ -372,9 +390,11 @@ def run_ours(args, rank, world, local) -> int:
     e2e_value = BATCH_VIEWS * args.steps / (e2e_ms * 1e-3)
 
     breakdown = None
+    stats = view_pair_stats(trainer, [trainer.views[vi] for vi in mine])
     if rank == 0:
         v2 = scenes.config2(0, n=args.gaussians).views[0].as_dict(dev)
         breakdown = per_view_breakdown(trainer, v2)
+        breakdown.update({f"{k}_pairs": v for k, v in view_pair_stats(trainer, [v2]).items()})
     barrier(world)
     if rank != 0:
         return 0
@@ -387,12 +407,14 @@ def run_ours(args, rank, world, local) -> int:
                    "resolution": "1920x1080", "parallelism": f"views sharded over {world} rank(s)",
                    "l2": "inputs larger than L2 (236 MB of parameters + 25 MB per target)"},
         "per_view_config2": breakdown,
+        "stage_ms_per_view": stage_ms,
+        "views_pairs": stats,
         "gpu_launches": total_launches,
         "gpu_launches_per_rank": launches,
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d_bytes * world,
                 "d2h_bytes_per_step": 4 * world},
-        "roofline": roofline_entry(breakdown, pk, args.gaussians),
+        "roofline": roofline_entry(stage_ms, stats, args.steps * len(mine), pk, args.gaussians),
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(sc, sc.views[0], targets[0])

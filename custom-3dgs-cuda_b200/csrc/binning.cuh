@@ -138,7 +138,7 @@ __device__ __forceinline__ void bin_block(const BinParams& p, int tile, int i, u
   }
 }
 
-__global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
+static __global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
   __shared__ unsigned s_tile, s_prefix;
   __shared__ unsigned s_scan[33];
   __shared__ unsigned s_hist[4][256];
@@ -186,7 +186,7 @@ struct DupParams {
 // (the order of csrc/forward/rasterize.cu:124-135). A block's pairs are contiguous, so
 // the block writes them cooperatively: pair p belongs to the Gaussian whose exclusive
 // offset is the last one <= p.
-__global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p) {
+static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p) {
   __shared__ unsigned s_tile, s_prefix;
   __shared__ unsigned s_scan[33];
   __shared__ unsigned s_off[kBinThreads];
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p
 
 // Tile ranges from the tile-sorted keys (csrc/forward/rasterize.cu:146-165); ranges of
 // tiles with no pairs stay (0, 0) from the preceding memset.
-__global__ void __launch_bounds__(256) tile_ranges_kernel(const unsigned* __restrict__ keys,
+static __global__ void __launch_bounds__(256) tile_ranges_kernel(const unsigned* __restrict__ keys,
                                                           const int* pair_count,
                                                           long long pair_capacity,
                                                           unsigned num_tiles,

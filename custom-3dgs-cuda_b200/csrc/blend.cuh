@@ -48,7 +48,7 @@ struct BlendFwdParams {
 // alpha = min(0.99, o * exp(power)), skipped when power > 0 or alpha < 1/255; colour
 // accumulates c * alpha * T and T *= 1 - alpha; the pixel stops after the Gaussian that
 // takes T below 1e-4. n_contrib counts Gaussians walked up to the last one applied.
-__global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(BlendFwdParams p) {
+static __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(BlendFwdParams p) {
   __shared__ float4 s_rec[2][3][kBlendBatch];
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
@@ -135,6 +135,7 @@ struct BlendBwdParams {
   float* g_cov2d;
   float* g_colors;
   float* g_alpha;
+  float4* g_accum;  // fused mode: 3 float4 per Gaussian (see blend_backward_kernel)
 };
 
 // Butterfly reduce-scatter of 9 per-lane values over a warp in 12 shuffles. On return the
@@ -194,6 +195,14 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // into a per-batch shared slot; after each batch the slot sums are converted from
 // dL/dconic to dL/dSigma2 = -V G V (V the conic, G its symmetric gradient) and added to
 // the global gradients with one atomic per component.
+//
+// kFusedAccum selects the flush: false converts each tile's dL/dconic to dL/dSigma2 and adds
+// into the four reference-layout gradient arrays (9 scalar atomics, as the reference does);
+// true adds the raw sums into g_accum with vector atomics, 3 float4 per Gaussian:
+//   [0] = (dmean.x, dmean.y, dconic.x, dconic.y), [1] = (dconic.z, dopacity, dcol.r, dcol.g),
+//   [2] = (dcol.b, -, -, -), and the conversion happens once per Gaussian later
+//   (dL/dSigma2 is linear in dL/dconic for a fixed conic, so the sums commute with it).
+template <bool kFusedAccum>
 __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdParams p) {
   __shared__ float4 s_rec[2][3][kBlendBatch];
   __shared__ float s_acc[kBlendBatch * kAccStride];
@@ -319,7 +328,12 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
       bool any = false;
 #pragma unroll
       for (int q = 0; q < 9; ++q) any |= acc[q] != 0.0f;
-      if (any && g >= 0 && g < p.N) {
+      if (kFusedAccum && any && g >= 0 && g < p.N) {
+        float4* dst = p.g_accum + 3 * (size_t)g;
+        atomicAdd(dst, make_float4(acc[0], acc[1], acc[2], acc[3]));
+        atomicAdd(dst + 1, make_float4(acc[4], acc[8], acc[5], acc[6]));
+        atomicAdd(&dst[2].x, acc[7]);
+      } else if (any && g >= 0 && g < p.N) {
         atomicAdd(p.g_mean2d + 2 * g, acc[0]);
         atomicAdd(p.g_mean2d + 2 * g + 1, acc[1]);
         const float vx = rec[0][tid].z, vy = rec[0][tid].w, vz = rec[1][tid].x;

@@ -14,6 +14,15 @@ static std::atomic<unsigned long long> g_launches{0};
 
 void count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+static constexpr int kMaxStageEvents = 16;
+static std::atomic<int> g_stage_n{0};
+static cudaEvent_t g_stage_events[kMaxStageEvents] = {};
+
+void mark_stage(int k, cudaStream_t stream) {
+  if (k < g_stage_n.load(std::memory_order_acquire) && g_stage_events[k])
+    cudaEventRecord(g_stage_events[k], stream);
+}
+
 int set_error(int code, const std::string& msg) {
   t_last_error = msg;
   return code;
@@ -70,6 +79,35 @@ extern "C" int gs_event_synchronize(void* event) {
 extern "C" int gs_event_destroy(void* event) {
   GS_API_BEGIN();
   if (event) GS_CUDA(cudaEventDestroy((cudaEvent_t)event));
+  return GS_OK;
+  GS_API_END();
+}
+
+extern "C" int gs_set_stage_events(void* const* events, int n) {
+  GS_API_BEGIN();
+  GS_REQUIRE(n >= 0 && n <= gs::kMaxStageEvents, "at most 16 stage events");
+  gs::g_stage_n.store(0, std::memory_order_release);
+  if (events == nullptr || n == 0) return GS_OK;
+  for (int k = 0; k < n; ++k) gs::g_stage_events[k] = (cudaEvent_t)events[k];
+  gs::g_stage_n.store(n, std::memory_order_release);
+  return GS_OK;
+  GS_API_END();
+}
+
+extern "C" int gs_event_create_timed(void** event) {
+  GS_API_BEGIN();
+  GS_REQUIRE(event != nullptr, "null pointer");
+  cudaEvent_t ev = nullptr;
+  GS_CUDA(cudaEventCreate(&ev));
+  *event = ev;
+  return GS_OK;
+  GS_API_END();
+}
+
+extern "C" int gs_event_elapsed_ms(void* start, void* end, float* ms) {
+  GS_API_BEGIN();
+  GS_REQUIRE(start && end && ms, "null pointer");
+  GS_CUDA(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));
   return GS_OK;
   GS_API_END();
 }

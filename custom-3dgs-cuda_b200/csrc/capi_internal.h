@@ -13,6 +13,9 @@ namespace gs {
 // Counts kernel launches made by this library (read by gs_kernel_launches).
 void count_launches(unsigned n);
 
+// Records the installed stage event `k` (gs_set_stage_events) on `stream`, if any.
+void mark_stage(int k, cudaStream_t stream);
+
 // Records `msg` as the calling thread's last error and returns `code`.
 int set_error(int code, const std::string& msg);
 void clear_error();

@@ -30,7 +30,7 @@ struct SortPass {
   int shift;                   // bit offset of this pass's digit
 };
 
-__global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(SortPass a) {
+static __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(SortPass a) {
   __shared__ unsigned s_tile;
   __shared__ unsigned s_warp_hist[kSortWarps][kRadix];
   __shared__ unsigned s_local_start[kRadix];

@@ -6,7 +6,7 @@
 #include "blend.cuh"
 #include "capi_internal.h"
 #include "onesweep.cuh"
-#include "raster_layout.h"
+#include "raster_internal.h"
 
 namespace gs {
 
@@ -84,16 +84,38 @@ static int sm_count() {
   return count;
 }
 
-int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* depths,
-                     const float* mean2d, const float* cov2d, const float* colors,
-                     const float* alpha, char* ws, long long capacity, float* img,
-                     int* sorted_ids, int* tile_ranges, float* final_T, int* n_contrib,
-                     int* pair_count_dev, int* pair_count_host, cudaEvent_t m_ready,
-                     cudaStream_t stream) {
+void fill_bin_params(BinParams& bp, const RasterLayout& L, char* ws, int N, int H, int W,
+                     const float* depths, const float* mean2d, const float* cov2d,
+                     const float* colors, const float* alpha, long long capacity) {
   RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
-  GS_CUDA(cudaMemsetAsync(ws, 0, L.zero_bytes, stream));
-  GS_CUDA(cudaMemsetAsync(tile_ranges, 0, (size_t)L.T * 2 * sizeof(int), stream));
-  uint2* rects = reinterpret_cast<uint2*>(ws + L.rects);
+  bp.N = N;
+  bp.W = W;
+  bp.H = H;
+  bp.tiles_x = L.tiles_x;
+  bp.tiles_y = L.tiles_y;
+  bp.depths = depths;
+  bp.mean2d = mean2d;
+  bp.cov2d = cov2d;
+  bp.colors = colors;
+  bp.alpha = alpha;
+  bp.rects = reinterpret_cast<uint2*>(ws + L.rects);
+  bp.records = reinterpret_cast<float4*>(ws + L.records);
+  bp.depth_keys = reinterpret_cast<unsigned*>(ws + L.depth_keys[0]);
+  bp.depth_vals = reinterpret_cast<unsigned*>(ws + L.depth_vals[0]);
+  bp.status = reinterpret_cast<unsigned*>(ws + L.status_bin);
+  bp.ticket = &hdr->ticket_bin;
+  bp.done_counter = &hdr->done_bin;
+  bp.depth_hist = reinterpret_cast<unsigned*>(ws + L.depth_hist);
+  bp.pair_acc = &hdr->pair_acc;
+  bp.n_visible = &hdr->n_visible;
+  bp.pair_count = &hdr->pair_count;
+  bp.pair_capacity = capacity;
+}
+
+int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
+                          long long capacity, float* img, int* sorted_ids, int* tile_ranges,
+                          float* final_T, int* n_contrib, cudaStream_t stream) {
+  RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
   float4* records = reinterpret_cast<float4*>(ws + L.records);
   unsigned* dk[2] = {reinterpret_cast<unsigned*>(ws + L.depth_keys[0]),
                      reinterpret_cast<unsigned*>(ws + L.depth_keys[1])};
@@ -105,41 +127,6 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
   unsigned* tv[2];
   tv[P % 2] = reinterpret_cast<unsigned*>(sorted_ids);
   tv[(P + 1) % 2] = reinterpret_cast<unsigned*>(ws + L.tile_vals_tmp);
-
-  if (N > 0) {
-    BinParams bp;
-    bp.N = N;
-    bp.W = W;
-    bp.H = H;
-    bp.tiles_x = L.tiles_x;
-    bp.tiles_y = L.tiles_y;
-    bp.depths = depths;
-    bp.mean2d = mean2d;
-    bp.cov2d = cov2d;
-    bp.colors = colors;
-    bp.alpha = alpha;
-    bp.rects = rects;
-    bp.records = records;
-    bp.depth_keys = dk[0];
-    bp.depth_vals = dv[0];
-    bp.status = reinterpret_cast<unsigned*>(ws + L.status_bin);
-    bp.ticket = &hdr->ticket_bin;
-    bp.done_counter = &hdr->done_bin;
-    bp.depth_hist = reinterpret_cast<unsigned*>(ws + L.depth_hist);
-    bp.pair_acc = &hdr->pair_acc;
-    bp.n_visible = &hdr->n_visible;
-    bp.pair_count = &hdr->pair_count;
-    bp.pair_capacity = capacity;
-    bin_prepare_kernel<<<(unsigned)L.nb, kBinThreads, 0, stream>>>(bp);
-    GS_CHECK_LAUNCH();
-  }
-  if (pair_count_dev)
-    GS_CUDA(cudaMemcpyAsync(pair_count_dev, &hdr->pair_count, sizeof(int),
-                            cudaMemcpyDeviceToDevice, stream));
-  if (pair_count_host)
-    GS_CUDA(cudaMemcpyAsync(pair_count_host, &hdr->pair_count, sizeof(int),
-                            cudaMemcpyDeviceToHost, stream));
-  if (m_ready) GS_CUDA(cudaEventRecord(m_ready, stream));
 
   if (N > 0) {
     // depth sort of the visible Gaussians: 4 passes, result back in buffer 0
@@ -159,6 +146,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
       onesweep_pass_kernel<<<(unsigned)L.nd, kSortThreads, 0, stream>>>(sp);
       GS_CHECK_LAUNCH();
     }
+    mark_stage(2, stream);
     DupParams dp;
     dp.tiles_x = L.tiles_x;
     dp.n_tile_passes = P;
@@ -166,7 +154,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
     dp.pair_count = &hdr->pair_count;
     dp.pair_capacity = capacity;
     dp.sorted_gids = dv[0];
-    dp.rects = rects;
+    dp.rects = reinterpret_cast<uint2*>(ws + L.rects);
     dp.status = reinterpret_cast<unsigned*>(ws + L.status_dup);
     dp.ticket = &hdr->ticket_dup;
     dp.tile_keys = tk[0];
@@ -174,6 +162,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
     dp.tile_hist = reinterpret_cast<unsigned*>(ws + L.tile_hist);
     scan_duplicate_kernel<<<(unsigned)L.nb, kBinThreads, 0, stream>>>(dp);
     GS_CHECK_LAUNCH();
+    mark_stage(3, stream);
     for (int pass = 0; pass < P; ++pass) {
       SortPass sp;
       sp.keys_in = tk[pass & 1];
@@ -192,6 +181,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
         GS_CHECK_LAUNCH();
       }
     }
+    mark_stage(4, stream);
     if (capacity > 0) {
       const long long blocks = std::min<long long>((capacity + 255) / 256, (long long)sm_count() * 8);
       tile_ranges_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
@@ -200,6 +190,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
       GS_CHECK_LAUNCH();
     }
   }
+  mark_stage(5, stream);
   BlendFwdParams fp;
   fp.W = W;
   fp.H = H;
@@ -214,7 +205,34 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
   fp.n_contrib = n_contrib;
   blend_forward_kernel<<<(unsigned)L.T, kBlendThreads, 0, stream>>>(fp);
   GS_CHECK_LAUNCH();
+  mark_stage(6, stream);
   return GS_OK;
+}
+
+int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* depths,
+                     const float* mean2d, const float* cov2d, const float* colors,
+                     const float* alpha, char* ws, long long capacity, float* img,
+                     int* sorted_ids, int* tile_ranges, float* final_T, int* n_contrib,
+                     int* pair_count_dev, int* pair_count_host, cudaEvent_t m_ready,
+                     cudaStream_t stream) {
+  RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
+  GS_CUDA(cudaMemsetAsync(ws, 0, L.zero_bytes, stream));
+  GS_CUDA(cudaMemsetAsync(tile_ranges, 0, (size_t)L.T * 2 * sizeof(int), stream));
+  if (N > 0) {
+    BinParams bp;
+    fill_bin_params(bp, L, ws, N, H, W, depths, mean2d, cov2d, colors, alpha, capacity);
+    bin_prepare_kernel<<<(unsigned)L.nb, kBinThreads, 0, stream>>>(bp);
+    GS_CHECK_LAUNCH();
+  }
+  if (pair_count_dev)
+    GS_CUDA(cudaMemcpyAsync(pair_count_dev, &hdr->pair_count, sizeof(int),
+                            cudaMemcpyDeviceToDevice, stream));
+  if (pair_count_host)
+    GS_CUDA(cudaMemcpyAsync(pair_count_host, &hdr->pair_count, sizeof(int),
+                            cudaMemcpyDeviceToHost, stream));
+  if (m_ready) GS_CUDA(cudaEventRecord(m_ready, stream));
+  return launch_sort_and_blend(L, N, H, W, ws, capacity, img, sorted_ids, tile_ranges, final_T,
+                               n_contrib, stream);
 }
 
 }  // namespace gs
@@ -296,7 +314,8 @@ extern "C" int gs_rasterize_backward(int N, int H, int W, const float* grad_img,
   bp.g_cov2d = g_cov2d;
   bp.g_colors = g_colors;
   bp.g_alpha = g_alpha;
-  blend_backward_kernel<<<(unsigned)(tiles_x * tiles_y), kBlendThreads, 0, st>>>(bp);
+  bp.g_accum = nullptr;
+  blend_backward_kernel<false><<<(unsigned)(tiles_x * tiles_y), kBlendThreads, 0, st>>>(bp);
   GS_CHECK_LAUNCH();
   return GS_OK;
   GS_API_END();

@@ -1,0 +1,362 @@
+// Fused render path used by RasterizeFunction: the whole forward of one view from the
+// Gaussian parameters (gs_render_forward) and the whole backward to the parameter gradients
+// (gs_render_backward). Same device functions, hence the same results, as the per-op entry
+// points; the intermediates mean2d / cov2d / depths / colours never go through HBM.
+//
+// Forward: render_preprocess_kernel (projection + SH colour + screen radius + binning prep,
+// one thread per Gaussian, SH rows staged warp-wide) followed by the shared depth sort, pair
+// duplication, tile sort, tile ranges and blend of launch_sort_and_blend.
+// Backward: blend_backward_kernel<true> accumulates raw per-Gaussian sums (mean, conic,
+// opacity, colour gradients) with vector atomics; render_gaussian_backward_kernel then, per
+// Gaussian, converts dL/dconic to dL/dSigma2 once, runs the SH and projection backward and
+// writes (or accumulates into) the six parameter gradients and dL/dmean2d.
+#include "binning.cuh"
+#include "blend.cuh"
+#include "capi_internal.h"
+#include "gaussian_ops.cuh"
+#include "onesweep.cuh"
+#include "projection.cuh"
+#include "raster_internal.h"
+#include "sh.cuh"
+
+namespace gs {
+
+// torch's radius formula of the reference wrapper (rasterize.py:49-53), op by op with
+// round-to-nearest intrinsics (no contraction) so that it matches torch bit for bit:
+// mid = 0.5 (a + c); r = mid + sqrt(clamp(((a - c) / 2)^2 + b^2, min 0.1));
+// radius = 3 sqrt(clamp(r, min 0)). clamp keeps NaN as torch does.
+__device__ __forceinline__ float torch_clamp_min(float x, float m) {
+  return (x != x) ? x : fmaxf(x, m);
+}
+__device__ __forceinline__ float screen_radius(float a, float b, float c) {
+  const float mid = __fmul_rn(0.5f, __fadd_rn(a, c));
+  const float h = __fmul_rn(0.5f, __fsub_rn(a, c));
+  const float r2 = __fadd_rn(__fmul_rn(h, h), __fmul_rn(b, b));
+  const float r = __fadd_rn(mid, __fsqrt_rn(torch_clamp_min(r2, 0.1f)));
+  return __fmul_rn(3.0f, __fsqrt_rn(torch_clamp_min(r, 0.0f)));
+}
+
+struct PreprocessParams {
+  BinParams bin;
+  const float *mu, *q, *s, *opacity, *albedo, *k_j, *R, *t, *cam_pos;
+  float fx, fy, cx, cy;
+  float* radii;
+};
+
+constexpr size_t kPreprocessSmem = 8 * 32 * kShRestFloats * sizeof(float);
+
+__global__ void __launch_bounds__(kBinThreads) render_preprocess_kernel(PreprocessParams pp) {
+  __shared__ unsigned s_tile, s_prefix;
+  __shared__ unsigned s_scan[33];
+  __shared__ unsigned s_hist[4][256];
+  __shared__ bool s_last;
+  extern __shared__ __align__(16) float s_stage[];  // [8 warps][32 * 45]
+  const BinParams& p = pp.bin;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
+  for (int k = tid; k < 4 * 256; k += kBinThreads) (&s_hist[0][0])[k] = 0u;
+  __syncthreads();
+  const int tile = (int)s_tile;
+  const int i = tile * kBinThreads + tid;
+
+  Camera cam;
+  load_camera(pp.R, pp.t, pp.fx, pp.fy, pp.cx, pp.cy, cam);
+  Projected pr;
+  unsigned count = 0, depth_bits = 0;
+  float3 m = make_float3(0.f, 0.f, 0.f);
+  if (i < p.N) {
+    m = make_float3(__ldg(pp.mu + 3 * i), __ldg(pp.mu + 3 * i + 1), __ldg(pp.mu + 3 * i + 2));
+    const float4 qi = make_float4(__ldg(pp.q + 4 * i), __ldg(pp.q + 4 * i + 1),
+                                  __ldg(pp.q + 4 * i + 2), __ldg(pp.q + 4 * i + 3));
+    const float3 si =
+        make_float3(__ldg(pp.s + 3 * i), __ldg(pp.s + 3 * i + 1), __ldg(pp.s + 3 * i + 2));
+    const bool front = project_gaussian(cam, m.x, m.y, m.z, qi, si, pr);
+    pp.radii[i] = screen_radius(pr.cov.x, pr.cov.y, pr.cov.z);
+    TileRect r;
+    if (front && splat_tile_rect(pr.mean, pr.cov.x, pr.cov.y, pr.cov.z, p.W, p.H, p.tiles_x,
+                                 p.tiles_y, r))
+      count = (unsigned)rect_count(r);
+  }
+  // SH colour only for splats that cover a tile; the warp stages its SH rows if any lane does
+  if (__ballot_sync(0xffffffffu, count > 0)) {
+    float* stage = s_stage + warp * 32 * kShRestFloats;
+    warp_load_rows<kShRestFloats>(pp.k_j, tile * kBinThreads + warp * 32, p.N, stage);
+    if (count > 0) {
+      float kj[kShRestFloats];
+#pragma unroll
+      for (int k = 0; k < kShRestFloats; ++k) kj[k] = stage[lane * kShRestFloats + k];
+      const float3 cp = make_float3(__ldg(pp.cam_pos), __ldg(pp.cam_pos + 1), __ldg(pp.cam_pos + 2));
+      const float3 A = make_float3(__ldg(pp.albedo + 3 * i), __ldg(pp.albedo + 3 * i + 1),
+                                   __ldg(pp.albedo + 3 * i + 2));
+      const float3 d = sh_forward_direction(m, cp);
+      float Y[kShRest];
+      sh_basis(d.x, d.y, d.z, Y);
+      const float3 rgb = sh_unclamped(Y, A, kj);
+      const float3 col = make_float3(clamp01(rgb.x), clamp01(rgb.y), clamp01(rgb.z));
+      count = bin_gaussian(p, i, pr.mean, pr.cov.x, pr.cov.y, pr.cov.z, pr.depth, col,
+                           __ldg(pp.opacity + i), depth_bits);
+    }
+  }
+  bin_block(p, tile, i, count, depth_bits, s_scan, s_hist, s_prefix, s_last);
+}
+
+struct GaussianBwdParams {
+  int N;
+  const float4* accum;    // 3 per Gaussian from blend_backward_kernel<true>
+  const float4* records;  // forward blend records (conic)
+  const float *mu, *q, *s, *albedo, *k_j, *R, *t, *cam_pos;
+  float fx, fy, cx, cy;
+  float *g_mu, *g_q, *g_s, *g_opacity, *g_albedo, *g_k_j, *g_mean2d;
+  int accumulate;
+};
+
+template <int F>
+__device__ __forceinline__ void warp_add_rows(float* __restrict__ dst, int row0, int n_rows,
+                                              const float* stage) {
+  const int lane = threadIdx.x & 31;
+  const int n = min(32, n_rows - row0) * F;
+  float* base = dst + (size_t)row0 * F;
+  for (int i = lane; i < n; i += 32) base[i] += stage[i];
+}
+
+__device__ __forceinline__ void put(float* p, float v, bool acc) {
+  if (acc) *p += v; else *p = v;
+}
+
+__global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianBwdParams p) {
+  extern __shared__ __align__(16) float s_stage[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = blockIdx.x * blockDim.x + warp * 32;
+  if (row0 >= p.N) return;
+  const int i = row0 + lane;
+  const bool valid = i < p.N;
+  float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, a2 = a0;
+  if (valid) {
+    a0 = p.accum[3 * i];
+    a1 = p.accum[3 * i + 1];
+    a2 = p.accum[3 * i + 2];
+  }
+  const bool touched = a0.x != 0.f || a0.y != 0.f || a0.z != 0.f || a0.w != 0.f ||
+                       a1.x != 0.f || a1.y != 0.f || a1.z != 0.f || a1.w != 0.f || a2.x != 0.f;
+  const bool acc = p.accumulate != 0;
+  float* stage = s_stage + warp * 32 * kShRestFloats;
+  const bool warp_touched = __ballot_sync(0xffffffffu, touched) != 0u;
+  if (warp_touched) warp_load_rows<kShRestFloats>(p.k_j, row0, p.N, stage);
+  float gkj[kShRestFloats];
+#pragma unroll
+  for (int k = 0; k < kShRestFloats; ++k) gkj[k] = 0.f;
+  if (valid && touched) {
+    float kj[kShRestFloats];
+#pragma unroll
+    for (int k = 0; k < kShRestFloats; ++k) kj[k] = stage[lane * kShRestFloats + k];
+    // dL/dconic -> dL/dSigma2 = -V G V with G's off-diagonal half of the packed sum
+    const float4 r0 = p.records[3 * i], r1 = p.records[3 * i + 1];
+    const float vx = r0.z, vy = r0.w, vz = r1.x;
+    const float gx = a0.z, gy = 0.5f * a0.w, gz = a1.x;
+    const float3 gcov = make_float3(-(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz),
+                                    -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz),
+                                    -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz));
+    const float2 gmean = make_float2(a0.x, a0.y);
+    const float3 gcol = make_float3(a1.z, a1.w, a2.x);
+    Camera cam;
+    load_camera(p.R, p.t, p.fx, p.fy, p.cx, p.cy, cam);
+    const float3 m = make_float3(__ldg(p.mu + 3 * i), __ldg(p.mu + 3 * i + 1), __ldg(p.mu + 3 * i + 2));
+    const float4 qi = make_float4(__ldg(p.q + 4 * i), __ldg(p.q + 4 * i + 1),
+                                  __ldg(p.q + 4 * i + 2), __ldg(p.q + 4 * i + 3));
+    const float3 si = make_float3(__ldg(p.s + 3 * i), __ldg(p.s + 3 * i + 1), __ldg(p.s + 3 * i + 2));
+    ProjectionGrad pg;
+    project_gaussian_backward(cam, m.x, m.y, m.z, qi, si, gmean, gcov, pg);
+    const float3 cp = make_float3(__ldg(p.cam_pos), __ldg(p.cam_pos + 1), __ldg(p.cam_pos + 2));
+    const float3 A = make_float3(__ldg(p.albedo + 3 * i), __ldg(p.albedo + 3 * i + 1),
+                                 __ldg(p.albedo + 3 * i + 2));
+    float3 gA;
+    const float3 gmu_sh = sh_backward(gcol, m, cp, A, kj, gA, gkj);
+    put(p.g_mu + 3 * i, pg.mu.x + gmu_sh.x, acc);
+    put(p.g_mu + 3 * i + 1, pg.mu.y + gmu_sh.y, acc);
+    put(p.g_mu + 3 * i + 2, pg.mu.z + gmu_sh.z, acc);
+    put(p.g_q + 4 * i, pg.q.x, acc);
+    put(p.g_q + 4 * i + 1, pg.q.y, acc);
+    put(p.g_q + 4 * i + 2, pg.q.z, acc);
+    put(p.g_q + 4 * i + 3, pg.q.w, acc);
+    put(p.g_s + 3 * i, pg.s.x, acc);
+    put(p.g_s + 3 * i + 1, pg.s.y, acc);
+    put(p.g_s + 3 * i + 2, pg.s.z, acc);
+    put(p.g_opacity + i, a1.y, acc);
+    put(p.g_albedo + 3 * i, gA.x, acc);
+    put(p.g_albedo + 3 * i + 1, gA.y, acc);
+    put(p.g_albedo + 3 * i + 2, gA.z, acc);
+    if (p.g_mean2d) {
+      put(p.g_mean2d + 2 * i, gmean.x, acc);
+      put(p.g_mean2d + 2 * i + 1, gmean.y, acc);
+    }
+  } else if (valid && !acc) {
+    for (int k = 0; k < 3; ++k) p.g_mu[3 * i + k] = 0.f;
+    for (int k = 0; k < 4; ++k) p.g_q[4 * i + k] = 0.f;
+    for (int k = 0; k < 3; ++k) p.g_s[3 * i + k] = 0.f;
+    p.g_opacity[i] = 0.f;
+    for (int k = 0; k < 3; ++k) p.g_albedo[3 * i + k] = 0.f;
+    if (p.g_mean2d) p.g_mean2d[2 * i] = p.g_mean2d[2 * i + 1] = 0.f;
+  }
+  // SH-rest gradient rows: staged, then written (or added) coalesced
+  if (warp_touched || !acc) {
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < kShRestFloats; ++k) stage[lane * kShRestFloats + k] = gkj[k];
+    __syncwarp();
+    if (acc) warp_add_rows<kShRestFloats>(p.g_k_j, row0, p.N, stage);
+    else warp_store_rows<kShRestFloats>(p.g_k_j, row0, p.N, stage);
+  }
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" size_t gs_render_workspace_size(int N, int H, int W, long long pair_capacity) {
+  if (N < 0 || H <= 0 || W <= 0 || pair_capacity < 0) return 0;
+  return make_raster_layout(N, W, H, pair_capacity).total;
+}
+
+extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const float* q,
+                                 const float* s, const float* opacity, const float* albedo,
+                                 const float* k_j, const float* R, const float* t,
+                                 const float* cam_pos, float fx, float fy, float cx, float cy,
+                                 void* workspace, size_t workspace_bytes,
+                                 long long pair_capacity, float* img, int* sorted_ids,
+                                 int* tile_ranges, float* final_T, int* n_contrib, float* radii,
+                                 int* pair_count_host, void* m_ready_event, void* stream) {
+  GS_API_BEGIN();
+  GS_REQUIRE(N >= 0, "N must be non-negative");
+  GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
+  GS_REQUIRE((W + 15) / 16 < 65536 && (H + 15) / 16 < 65536, "image too large");
+  GS_REQUIRE(pair_capacity >= 0 && pair_capacity < (1ll << 30),
+             "pair capacity must be in [0, 2^30)");
+  GS_REQUIRE(img && tile_ranges && final_T && n_contrib && workspace, "null pointer");
+  GS_REQUIRE(N == 0 || (mu && q && s && opacity && albedo && k_j && R && t && cam_pos && radii),
+             "null input pointer");
+  GS_REQUIRE(pair_capacity == 0 || sorted_ids, "null sorted_ids with a non-zero capacity");
+  const RasterLayout L = make_raster_layout(N, W, H, pair_capacity);
+  GS_REQUIRE(workspace_bytes >= L.total, "workspace too small");
+  GS_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0u,
+             "workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
+  GS_CUDA(cudaMemsetAsync(ws, 0, L.zero_bytes, st));
+  GS_CUDA(cudaMemsetAsync(tile_ranges, 0, (size_t)L.T * 2 * sizeof(int), st));
+  mark_stage(0, st);
+  if (N > 0) {
+    PreprocessParams pp;
+    fill_bin_params(pp.bin, L, ws, N, H, W, nullptr, nullptr, nullptr, nullptr, nullptr,
+                    pair_capacity);
+    pp.mu = mu;
+    pp.q = q;
+    pp.s = s;
+    pp.opacity = opacity;
+    pp.albedo = albedo;
+    pp.k_j = k_j;
+    pp.R = R;
+    pp.t = t;
+    pp.cam_pos = cam_pos;
+    pp.fx = fx;
+    pp.fy = fy;
+    pp.cx = cx;
+    pp.cy = cy;
+    pp.radii = radii;
+    GS_CUDA(cudaFuncSetAttribute(render_preprocess_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kPreprocessSmem));
+    render_preprocess_kernel<<<(unsigned)L.nb, kBinThreads, kPreprocessSmem, st>>>(pp);
+    GS_CHECK_LAUNCH();
+  }
+  mark_stage(1, st);
+  if (pair_count_host)
+    GS_CUDA(cudaMemcpyAsync(pair_count_host, &hdr->pair_count, sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
+  if (m_ready_event) GS_CUDA(cudaEventRecord((cudaEvent_t)m_ready_event, st));
+  return launch_sort_and_blend(L, N, H, W, ws, pair_capacity, img, sorted_ids, tile_ranges,
+                               final_T, n_contrib, st);
+  GS_API_END();
+}
+
+extern "C" size_t gs_render_backward_workspace_size(int N) {
+  if (N < 0) return 0;
+  return (size_t)N * 3 * sizeof(float4) + 256;
+}
+
+extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, const float* mu,
+                                  const float* q, const float* s, const float* albedo,
+                                  const float* k_j, const float* R, const float* t,
+                                  const float* cam_pos, float fx, float fy, float cx, float cy,
+                                  const void* fwd_workspace, long long pair_capacity,
+                                  const int* sorted_ids, const int* tile_ranges,
+                                  const float* final_T, const int* n_contrib, void* workspace,
+                                  size_t workspace_bytes, float* g_mu, float* g_q, float* g_s,
+                                  float* g_opacity, float* g_albedo, float* g_k_j,
+                                  float* g_mean2d, int accumulate, void* stream) {
+  GS_API_BEGIN();
+  GS_REQUIRE(N >= 0, "N must be non-negative");
+  GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
+  if (N == 0) return GS_OK;
+  GS_REQUIRE(grad_img && mu && q && s && albedo && k_j && R && t && cam_pos && fwd_workspace &&
+                 tile_ranges && final_T && n_contrib && workspace && g_mu && g_q && g_s &&
+                 g_opacity && g_albedo && g_k_j,
+             "null pointer");
+  GS_REQUIRE(workspace_bytes >= gs_render_backward_workspace_size(N), "workspace too small");
+  const RasterLayout L = make_raster_layout(N, W, H, pair_capacity);
+  const float4* records =
+      reinterpret_cast<const float4*>(static_cast<const char*>(fwd_workspace) + L.records);
+  float4* accum = reinterpret_cast<float4*>(
+      (reinterpret_cast<uintptr_t>(workspace) + 255u) & ~uintptr_t(255u));
+  cudaStream_t st = (cudaStream_t)stream;
+  GS_CUDA(cudaMemsetAsync(accum, 0, (size_t)N * 3 * sizeof(float4), st));
+  mark_stage(7, st);
+  BlendBwdParams bp;
+  bp.N = N;
+  bp.W = W;
+  bp.H = H;
+  bp.tiles_x = L.tiles_x;
+  bp.grad_img = grad_img;
+  bp.ranges = reinterpret_cast<const int2*>(tile_ranges);
+  bp.sorted_ids = sorted_ids;
+  bp.records = records;
+  bp.final_T = final_T;
+  bp.n_contrib = n_contrib;
+  bp.g_mean2d = bp.g_cov2d = bp.g_colors = bp.g_alpha = nullptr;
+  bp.g_accum = accum;
+  blend_backward_kernel<true><<<(unsigned)L.T, kBlendThreads, 0, st>>>(bp);
+  GS_CHECK_LAUNCH();
+  mark_stage(8, st);
+  GaussianBwdParams gp;
+  gp.N = N;
+  gp.accum = accum;
+  gp.records = records;
+  gp.mu = mu;
+  gp.q = q;
+  gp.s = s;
+  gp.albedo = albedo;
+  gp.k_j = k_j;
+  gp.R = R;
+  gp.t = t;
+  gp.cam_pos = cam_pos;
+  gp.fx = fx;
+  gp.fy = fy;
+  gp.cx = cx;
+  gp.cy = cy;
+  gp.g_mu = g_mu;
+  gp.g_q = g_q;
+  gp.g_s = g_s;
+  gp.g_opacity = g_opacity;
+  gp.g_albedo = g_albedo;
+  gp.g_k_j = g_k_j;
+  gp.g_mean2d = g_mean2d;
+  gp.accumulate = accumulate;
+  GS_CUDA(cudaFuncSetAttribute(render_gaussian_backward_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kPreprocessSmem));
+  render_gaussian_backward_kernel<<<(N + 255) / 256, 256, kPreprocessSmem, st>>>(gp);
+  GS_CHECK_LAUNCH();
+  mark_stage(9, st);
+  return GS_OK;
+  GS_API_END();
+}

@@ -38,12 +38,23 @@ SIGNATURES = {
     "gs_sh_backward": (c_int, [c_int, P, P, P, P, P, P, P, P, P]),
     "gs_project_backward": (c_int, [c_int, P, P, P, P, P, P, P, c_float, c_float, c_float,
                                     c_float, P, P, P, P]),
+    "gs_render_workspace_size": (c_size_t, [c_int, c_int, c_int, c_longlong]),
+    "gs_render_forward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, c_float,
+                                  c_float, c_float, c_float, P, c_size_t, c_longlong, P, P, P,
+                                  P, P, P, P, P, P]),
+    "gs_render_backward_workspace_size": (c_size_t, [c_int]),
+    "gs_render_backward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, c_float,
+                                   c_float, c_float, c_float, P, c_longlong, P, P, P, P, P,
+                                   c_size_t, P, P, P, P, P, P, P, c_int, P]),
     "gs_l1_ssim_workspace_size": (c_size_t, [c_int, c_int]),
     "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),
+    "gs_set_stage_events": (c_int, [P, c_int]),
+    "gs_event_create_timed": (c_int, [POINTER(c_void_p)]),
+    "gs_event_elapsed_ms": (c_int, [P, P, POINTER(c_float)]),
     "gs_kernel_launches": (ctypes.c_ulonglong, []),
     "gs_device_error_bits": (c_int, [POINTER(c_uint)]),
     "gs_clear_device_errors": (c_int, []),
@@ -90,12 +101,20 @@ def clear_device_errors() -> None:
 
 
 class Event:
-    """A CUDA event owned by the library (timing disabled)."""
+    """A CUDA event owned by the library (timing disabled unless `timed`)."""
 
-    def __init__(self) -> None:
+    def __init__(self, timed: bool = False) -> None:
         h = c_void_p(0)
-        check(lib.gs_event_create(ctypes.byref(h)))
+        if timed:
+            check(lib.gs_event_create_timed(ctypes.byref(h)))
+        else:
+            check(lib.gs_event_create(ctypes.byref(h)))
         self.handle = h.value
+
+    def elapsed_ms(self, end: "Event") -> float:
+        ms = c_float(0.0)
+        check(lib.gs_event_elapsed_ms(self.handle, end.handle, ctypes.byref(ms)))
+        return float(ms.value)
 
     def synchronize(self) -> None:
         check(lib.gs_event_synchronize(self.handle))
@@ -106,3 +125,12 @@ class Event:
                 lib.gs_event_destroy(self.handle)
         except Exception:
             pass
+
+
+def set_stage_events(events: list["Event | None"] | None) -> None:
+    """Installs (or, with None, removes) the process-wide stage events of the render path."""
+    if not events:
+        check(lib.gs_set_stage_events(None, 0))
+        return
+    arr = (c_void_p * len(events))(*[e.handle if e is not None else None for e in events])
+    check(lib.gs_set_stage_events(arr, len(events)))

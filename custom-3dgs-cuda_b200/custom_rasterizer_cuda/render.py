@@ -1,0 +1,95 @@
+"""Fused render path over gs_render_forward / gs_render_backward (include/gs3d_b200.h).
+
+`render_forward` renders one view straight from the Gaussian parameters and returns the
+image, the screen radii and a `RenderState` that `render_backward` needs; `render_backward`
+returns (or accumulates into given buffers) the gradients of all six parameters. Outputs are
+identical to chaining project -> SH -> rasterize and their backwards, as the reference wrapper
+does (gaussian_splatting/rasterizer/rasterize.py:43-117).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _capacity, _m_event, _ptr, _stream, _tiles
+from ._lib import check, lib
+
+
+@dataclass
+class RenderState:
+    workspace: torch.Tensor
+    capacity: int
+    sorted_ids: torch.Tensor   # [capacity]; the first M are valid
+    pairs: int                 # M
+    tile_ranges: torch.Tensor
+    final_T: torch.Tensor
+    n_contrib: torch.Tensor
+    height: int
+    width: int
+
+
+def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy, height,
+                   width):
+    """(img[H,W,3], radii[N], RenderState). `opacity` is post-sigmoid, N or [N,1]."""
+    N, H, W = int(mu.shape[0]), int(height), int(width)
+    dev = mu.device
+    T = _tiles(H, W)
+    f32 = dict(device=dev, dtype=torch.float32)
+    i32 = dict(device=dev, dtype=torch.int32)
+    img = torch.empty((H, W, 3), **f32)
+    final_T = torch.empty((H, W), **f32)
+    n_contrib = torch.empty((H, W), **i32)
+    tile_ranges = torch.empty((T, 2), **i32)
+    radii = torch.empty((N,), **f32)
+    cap = _capacity.guess(N, H, W)
+    with torch.cuda.device(dev):
+        stream = _stream(dev)
+        m_host = torch.empty((1,), dtype=torch.int32, pin_memory=True)
+        ev = _m_event()
+        for _attempt in range(2):
+            ws_bytes = lib.gs_render_workspace_size(N, H, W, cap)
+            ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8)
+            sorted_ids = torch.empty((max(cap, 1),), **i32)
+            check(lib.gs_render_forward(
+                N, H, W, _ptr(mu), _ptr(q), _ptr(s), _ptr(opacity), _ptr(albedo), _ptr(k_j),
+                _ptr(R), _ptr(t), _ptr(cam_pos), float(fx), float(fy), float(cx), float(cy),
+                ws.data_ptr(), ws_bytes, cap, _ptr(img), sorted_ids.data_ptr(),
+                _ptr(tile_ranges), _ptr(final_T), _ptr(n_contrib), _ptr(radii),
+                m_host.data_ptr(), ev.handle, stream))
+            ev.synchronize()
+            M = int(m_host[0])
+            _capacity.update(N, H, W, M)
+            if M <= cap:
+                state = RenderState(ws, cap, sorted_ids, M, tile_ranges, final_T, n_contrib, H, W)
+                return img, radii, state
+            cap = M
+    raise RuntimeError("pair count kept growing between attempts")
+
+
+def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, cam_pos, fx, fy,
+                    cx, cy, want_mean2d_grad: bool = True, out=None):
+    """Gradients (mu, q, s, opacity[N], albedo, k_j, mean2d or None). With `out` (a tuple of
+    the first six buffers) the gradients are added into those buffers instead."""
+    N = int(mu.shape[0])
+    dev = mu.device
+    f32 = dict(device=dev, dtype=torch.float32)
+    accumulate = out is not None
+    if out is None:
+        out = (torch.empty((N, 3), **f32), torch.empty((N, 4), **f32), torch.empty((N, 3), **f32),
+               torch.empty((N,), **f32), torch.empty((N, 3), **f32),
+               torch.empty((N, 15, 3), **f32))
+    g_mean2d = torch.empty((N, 2), **f32) if want_mean2d_grad else None
+    grad_img = grad_img.contiguous()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.gs_render_backward_workspace_size(N)
+        ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8)
+        check(lib.gs_render_backward(
+            N, state.height, state.width, _ptr(grad_img), _ptr(mu), _ptr(q), _ptr(s),
+            _ptr(albedo), _ptr(k_j), _ptr(R), _ptr(t), _ptr(cam_pos), float(fx), float(fy),
+            float(cx), float(cy), state.workspace.data_ptr(), state.capacity,
+            state.sorted_ids.data_ptr(), _ptr(state.tile_ranges), _ptr(state.final_T),
+            _ptr(state.n_contrib), ws.data_ptr(), ws_bytes, *(_ptr(o) for o in out),
+            _ptr(g_mean2d), 1 if accumulate else 0, _stream(dev)))
+    return (*out, g_mean2d)

@@ -22,15 +22,12 @@ except ImportError:  # surfaced at first use, as in the reference
     crc = None
 
 
-def _screen_radii(cov_2d: t.Tensor) -> t.Tensor:
-    a, b, c = cov_2d[:, 0], cov_2d[:, 1], cov_2d[:, 2]
-    mid = 0.5 * (a + c)
-    radius = mid + t.sqrt(t.clamp((0.5 * (a - c)) ** 2 + b * b, min=0.1))
-    return (3.0 * t.sqrt(t.clamp(radius, min=0.0))).detach()
-
-
 class RasterizeFunction(t.autograd.Function):
-    """Projection -> SH colour -> tile binning/sort -> alpha blend, and the reverse."""
+    """Projection -> SH colour -> tile binning/sort -> alpha blend, and the reverse.
+
+    Runs the fused render path (custom_rasterizer_cuda.render: two C-ABI calls per direction
+    instead of the reference's six ops); its outputs equal chaining the six ops.
+    """
 
     last_mean2d_grad: t.Tensor | None = None
     last_radii2d: t.Tensor | None = None
@@ -43,51 +40,47 @@ class RasterizeFunction(t.autograd.Function):
                 "custom_rasterizer_cuda is not available; build it with "
                 "`python custom-3dgs-cuda_b200/build.py`"
             )
-        num_gaussians = mu.shape[0]
+        from custom_rasterizer_cuda.render import render_forward
+
         mu, q, s = mu.contiguous(), q.contiguous(), s.contiguous()
         alpha, albedo, k_j = alpha.contiguous(), albedo.contiguous(), k_j.contiguous()
         cam_rotation = cam_rotation.contiguous()
         cam_translation = cam_translation.contiguous()
+        for tensor, name in ((mu, "mu"), (q, "q"), (s, "s"), (alpha, "alpha"), (albedo, "albedo"),
+                             (k_j, "k_j"), (cam_rotation, "cam_rotation"),
+                             (cam_translation, "cam_translation")):
+            if not tensor.is_cuda or tensor.dtype != t.float32:
+                raise RuntimeError(f"{name} must be a CUDA FP32 tensor")
+        n = mu.shape[0]
+        if q.numel() < 4 * n or s.numel() < 3 * n or alpha.numel() != n or \
+                albedo.numel() < 3 * n or k_j.numel() < 45 * n:
+            raise RuntimeError("Gaussian parameters must hold N rows")
         fx_f, fy_f, cx_f, cy_f = float(fx), float(fy), float(cx), float(cy)
         img_h, img_w = int(height), int(width)
 
         cam_position = (-t.matmul(cam_rotation.T, cam_translation)).reshape(3).contiguous()
-        mean_2d, cov_2d, depths = crc.project(
-            num_gaussians, mu, q, s, cam_rotation, cam_translation, fx_f, fy_f, cx_f, cy_f
-        )
-        RasterizeFunction.last_radii2d = _screen_radii(cov_2d)
-        colors = crc.SH(num_gaussians, cam_position, mu, albedo, k_j)
-        rendered_img, sorted_ids, tile_ranges, final_T, n_contrib = crc.rasterize(
-            num_gaussians, depths, mean_2d, cov_2d, colors, alpha, img_h, img_w
-        )
-        ctx.save_for_backward(
-            mean_2d, cov_2d, colors, alpha, sorted_ids, tile_ranges, final_T, n_contrib,
-            mu, q, s, albedo, k_j, cam_rotation, cam_translation, cam_position,
-        )
-        ctx.num_gaussians = num_gaussians
-        ctx.height, ctx.width = img_h, img_w
+        img, radii, state = render_forward(mu, q, s, alpha, albedo, k_j, cam_rotation,
+                                           cam_translation, cam_position, fx_f, fy_f, cx_f, cy_f,
+                                           img_h, img_w)
+        RasterizeFunction.last_radii2d = radii
+        ctx.save_for_backward(mu, q, s, alpha, albedo, k_j, cam_rotation, cam_translation,
+                              cam_position)
+        ctx.state = state
         ctx.fx, ctx.fy, ctx.cx, ctx.cy = fx_f, fy_f, cx_f, cy_f
-        return rendered_img
+        return img
 
     @staticmethod
     def backward(ctx, grad_output):
-        (mean_2d, cov_2d, colors, alpha, sorted_ids, tile_ranges, final_T, n_contrib,
-         mu, q, s, albedo, k_j, cam_rotation, cam_translation, cam_position) = ctx.saved_tensors
-        mean_2d_grad, cov_2d_grad, colors_grad, alpha_grad = crc.backwards_rasterization(
-            grad_output.contiguous(), mean_2d, cov_2d, colors, alpha, sorted_ids, tile_ranges,
-            final_T, n_contrib, ctx.num_gaussians, ctx.height, ctx.width,
-        )
-        RasterizeFunction.last_mean2d_grad = mean_2d_grad.detach()
-        albedo_grad, k_j_grad, mu_sh_grad = crc.backwards_SH(
-            colors_grad, mu, albedo, k_j, cam_position
-        )
-        mu_grad, q_grad, s_grad = crc.backwards_projection(
-            mean_2d_grad, cov_2d_grad, mu, q, s, cam_rotation, cam_translation,
-            ctx.fx, ctx.fy, ctx.cx, ctx.cy,
-        )
-        mu_grad = mu_grad + mu_sh_grad
-        alpha_grad = alpha_grad.view_as(alpha) if alpha_grad.numel() == alpha.numel() else alpha_grad
-        return (mu_grad, q_grad, s_grad, alpha_grad, albedo_grad, k_j_grad,
+        from custom_rasterizer_cuda.render import render_backward
+
+        (mu, q, s, alpha, albedo, k_j, cam_rotation, cam_translation,
+         cam_position) = ctx.saved_tensors
+        g_mu, g_q, g_s, g_alpha, g_albedo, g_kj, g_mean2d = render_backward(
+            ctx.state, grad_output, mu, q, s, albedo, k_j, cam_rotation, cam_translation,
+            cam_position, ctx.fx, ctx.fy, ctx.cx, ctx.cy)
+        ctx.state = None
+        RasterizeFunction.last_mean2d_grad = g_mean2d
+        return (g_mu, g_q, g_s, g_alpha.view_as(alpha), g_albedo, g_kj,
                 None, None, None, None, None, None, None, None)
 
 

@@ -148,9 +148,10 @@ class Trainer:
         self.fg = FlatGrads(self.params, scene.N)
         self.fused_loss = fused_loss and device.type == "cuda"
 
-    def step(self, targets=None) -> torch.Tensor:
+    def step(self, targets=None, before_view=None) -> torch.Tensor:
         """One training step over this rank's share of the batch; returns the summed loss of
-        the local views (a 0-d tensor on the device)."""
+        the local views (a 0-d tensor on the device). `before_view(vi)`, if given, is called
+        before view vi is rendered (the benchmark installs its stage events there)."""
         from gaussian_splatting.rasterizer.rasterize import RasterizeFunction, rasterize
 
         targets = self.targets if targets is None else targets
@@ -159,6 +160,8 @@ class Trainer:
         total = torch.zeros((), device=self.device)
         for vi in self.plan.views():
             view = self.views[vi]
+            if before_view is not None:
+                before_view(vi)
             img = rasterize(self.gaussians, view)
             if self.fused_loss:
                 from gs3d_b200.loss import l1_ssim_loss

@@ -139,6 +139,42 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
                         float* g_s, void* stream);
 
 /*
+ * Fused render path (what RasterizeFunction runs): the six reference ops of one view in two
+ * calls. The reference wrapper chains project -> SH -> rasterize and their backwards
+ * (gaussian_splatting/rasterizer/rasterize.py:43-117); these give the same outputs without
+ * writing mean2d / cov2d / depths / colours to memory.
+ *
+ * gs_render_forward: opacity[N] (post-sigmoid), cam_pos = -R^T t (device, 3 floats, as the
+ * wrapper computes it). Outputs as gs_rasterize plus radii[N], the wrapper's screen radii
+ * 3 sqrt(max(mid + sqrt(max(((a-c)/2)^2 + b^2, 0.1)), 0)) (rasterize.py:49-53). The workspace
+ * (gs_render_workspace_size) must be kept for gs_render_backward, which reads the forward's
+ * blend records from it.
+ * gs_render_backward: gradients of every parameter (g_opacity w.r.t. the post-sigmoid
+ * opacity) and, when g_mean2d is non-NULL, dL/dmean2d. With accumulate = 0 the outputs are
+ * overwritten; otherwise the gradients are added to them.
+ */
+GS_API size_t gs_render_workspace_size(int N, int H, int W, long long pair_capacity);
+GS_API int gs_render_forward(int N, int H, int W, const float* mu, const float* q, const float* s,
+                             const float* opacity, const float* albedo, const float* k_j,
+                             const float* R, const float* t, const float* cam_pos, float fx,
+                             float fy, float cx, float cy, void* workspace,
+                             size_t workspace_bytes, long long pair_capacity, float* img,
+                             int* sorted_ids, int* tile_ranges, float* final_T, int* n_contrib,
+                             float* radii, int* pair_count_host, void* m_ready_event,
+                             void* stream);
+GS_API size_t gs_render_backward_workspace_size(int N);
+GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const float* mu,
+                              const float* q, const float* s, const float* albedo,
+                              const float* k_j, const float* R, const float* t,
+                              const float* cam_pos, float fx, float fy, float cx, float cy,
+                              const void* fwd_workspace, long long pair_capacity,
+                              const int* sorted_ids, const int* tile_ranges,
+                              const float* final_T, const int* n_contrib, void* workspace,
+                              size_t workspace_bytes, float* g_mu, float* g_q, float* g_s,
+                              float* g_opacity, float* g_albedo, float* g_k_j, float* g_mean2d,
+                              int accumulate, void* stream);
+
+/*
  * Fused photometric loss of the training step (no counterpart in the reference's extension;
  * the reference trainer computes it with torchmetrics, gaussian_splatting/utils/loss.py:12-33):
  * loss = (1 - lambda) * mean|img - target| + lambda * (1 - SSIM), SSIM with an 11x11 Gaussian
@@ -162,6 +198,19 @@ GS_API int gs_l1_ssim_backward(int H, int W, const float* img, const float* targ
 GS_API int gs_event_create(void** event);
 GS_API int gs_event_synchronize(void* event);
 GS_API int gs_event_destroy(void* event);
+
+/*
+ * Stage timing for profiling: while `events` (n cudaEvent_t handles, NULL entries allowed) is
+ * installed, gs_render_forward / gs_render_backward record events[k] on their stream at stage
+ * boundaries: 0 forward start, 1 after preprocess, 2 after the depth sort, 3 after pair
+ * duplication, 4 after the tile sort, 5 after tile ranges, 6 after the blend, 7 backward start
+ * (after the accumulator clear), 8 after the blend backward, 9 after the per-Gaussian
+ * backward. The setting is process-wide; events = NULL or n = 0 removes it. Timed events come
+ * from gs_event_create_timed and are read with gs_event_elapsed_ms.
+ */
+GS_API int gs_set_stage_events(void* const* events, int n);
+GS_API int gs_event_create_timed(void** event);
+GS_API int gs_event_elapsed_ms(void* start, void* end, float* ms);
 
 /* Number of kernels this library has launched in this process (all devices, all threads). */
 GS_API unsigned long long gs_kernel_launches(void);

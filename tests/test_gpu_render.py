@@ -1,0 +1,88 @@
+"""The fused render path (gs_render_forward / gs_render_backward, what RasterizeFunction runs)
+against the reference's chain of six ops through the same module: identical forward (image,
+contributor counts, transmittance, sorted ids, ranges), screen radii equal to the reference
+wrapper's torch expression bit for bit, gradients within 1e-4 relative."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from test_gpu_parity import assert_grad_close, np32, scenes_small
+
+pytestmark = pytest.mark.gpu
+
+
+def op_chain(crc, sc, view, dev, grad_img):
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    R, t = view.R.to(dev).contiguous(), view.T.to(dev).contiguous()
+    cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+    m2, c2, d = crc.project(sc.N, mu, q, s, R, t, view.fx, view.fy, view.cx, view.cy)
+    col = crc.SH(sc.N, cam, mu, A, kj)
+    op = torch.sigmoid(al).contiguous()
+    img, ids, ranges, fT, nc = crc.rasterize(sc.N, d, m2, c2, col, op, view.height, view.width)
+    gm, gc, gcol, ga = crc.backwards_rasterization(grad_img, m2, c2, col, op, ids, ranges, fT, nc,
+                                                   sc.N, view.height, view.width)
+    gA, gkj, gmu_sh = crc.backwards_SH(gcol, mu, A, kj, cam)
+    gmu, gq, gs = crc.backwards_projection(gm, gc, mu, q, s, R, t, view.fx, view.fy, view.cx,
+                                           view.cy)
+    a, b, c = c2[:, 0], c2[:, 1], c2[:, 2]
+    mid = 0.5 * (a + c)
+    radius = mid + torch.sqrt(torch.clamp((0.5 * (a - c)) ** 2 + b * b, min=0.1))
+    radii = 3.0 * torch.sqrt(torch.clamp(radius, min=0.0))
+    return dict(img=img, ids=ids, ranges=ranges, final_T=fT, n_contrib=nc, radii=radii,
+                grads=(gmu + gmu_sh, gq, gs, ga.reshape(-1), gA, gkj), mean2d_grad=gm)
+
+
+@pytest.mark.parametrize("case", list(scenes_small()), ids=lambda c: c[0])
+def test_fused_render_matches_op_chain(crc, cuda_device, case):
+    from custom_rasterizer_cuda.render import render_backward, render_forward
+
+    _, sc, view = case
+    dev = cuda_device
+    g = torch.Generator("cpu").manual_seed(11)
+    grad_img = torch.rand(view.height, view.width, 3, generator=g).to(dev)
+    ref = op_chain(crc, sc, view, dev, grad_img)
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    R, t = view.R.to(dev).contiguous(), view.T.to(dev).contiguous()
+    cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+    op = torch.sigmoid(al).contiguous()
+    img, radii, st = render_forward(mu, q, s, op, A, kj, R, t, cam, view.fx, view.fy, view.cx,
+                                    view.cy, view.height, view.width)
+    assert torch.equal(img, ref["img"])
+    assert torch.equal(st.final_T, ref["final_T"]) and torch.equal(st.n_contrib, ref["n_contrib"])
+    assert torch.equal(st.sorted_ids[:st.pairs], ref["ids"])
+    assert torch.equal(st.tile_ranges, ref["ranges"])
+    assert torch.equal(radii, ref["radii"])
+    grads = render_backward(st, grad_img, mu, q, s, A, kj, R, t, cam, view.fx, view.fy, view.cx,
+                            view.cy)
+    for mine, theirs, what in zip(grads[:6], ref["grads"], ("mu", "q", "s", "opacity", "A", "kj")):
+        assert_grad_close(np32(mine), np32(theirs), what)
+    assert_grad_close(np32(grads[6]), np32(ref["mean2d_grad"]), "mean2d")
+
+    # accumulate mode adds into the given buffers
+    bufs = tuple(torch.ones_like(x) for x in grads[:6])
+    render_backward(st, grad_img, mu, q, s, A, kj, R, t, cam, view.fx, view.fy, view.cx, view.cy,
+                    want_mean2d_grad=False, out=bufs)
+    for acc, fresh, what in zip(bufs, grads[:6], ("mu", "q", "s", "opacity", "A", "kj")):
+        assert_grad_close(np32(acc) - 1.0, np32(fresh), what + " (accumulated)")
+
+
+def test_rasterize_function_attributes(cuda_device):
+    """RasterizeFunction keeps the reference's class attributes: last_radii2d after the
+    forward, last_mean2d_grad after the backward."""
+    from gaussian_splatting.rasterizer.rasterize import RasterizeFunction, rasterize
+    from gaussian_splatting.scene.gaussian import gaussian
+    from gs3d_b200 import scenes
+
+    sc = scenes.config0(0)
+    g = gaussian(sc.N)
+    for name, p in zip(("mu", "q", "s", "alpha", "A", "k_j"), sc.params()):
+        setattr(g, name, p.to(cuda_device).requires_grad_(True))
+    img = rasterize(g, sc.views[0].as_dict(cuda_device))
+    assert RasterizeFunction.last_radii2d.shape == (sc.N,)
+    assert RasterizeFunction.last_mean2d_grad is None
+    img.sum().backward()
+    assert RasterizeFunction.last_mean2d_grad.shape == (sc.N, 2)
+    assert g.alpha.grad.shape == g.alpha.shape and torch.isfinite(g.alpha.grad).all()
