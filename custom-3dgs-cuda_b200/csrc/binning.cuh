@@ -34,9 +34,9 @@ __device__ __forceinline__ TileRect unpack_rect(uint2 p) {
 }
 
 // Per-Gaussian blend record, 3 x float4:
-//   [0] = (mean.x, mean.y, conic.x, conic.y)
-//   [1] = (conic.z, opacity, r, g)
-//   [2] = (b, gaussian index as bits, 0, 0)
+//   [0] = (mean.x, mean.y, extent.x, extent.y)   (extent: splat_extent)
+//   [1] = (conic.x, conic.y, conic.z, opacity)
+//   [2] = (r, g, b, gaussian index as bits)
 struct BinParams {
   int N, W, H, tiles_x, tiles_y;
   const float* depths;
@@ -73,9 +73,10 @@ __device__ __forceinline__ unsigned bin_gaussian(const BinParams& p, int i, floa
     if (count > 0) {
       p.rects[i] = pack_rect(r);
       const float3 conic = conic_from_cov(a, b, c);
-      p.records[3 * i + 0] = make_float4(mean.x, mean.y, conic.x, conic.y);
-      p.records[3 * i + 1] = make_float4(conic.z, opacity, color.x, color.y);
-      p.records[3 * i + 2] = make_float4(color.z, __int_as_float(i), 0.0f, 0.0f);
+      const float2 ext = splat_extent(conic, opacity);
+      p.records[3 * i + 0] = make_float4(mean.x, mean.y, ext.x, ext.y);
+      p.records[3 * i + 1] = make_float4(conic.x, conic.y, conic.z, opacity);
+      p.records[3 * i + 2] = make_float4(color.x, color.y, color.z, __int_as_float(i));
       depth_bits = __float_as_uint(depth);
     }
   }

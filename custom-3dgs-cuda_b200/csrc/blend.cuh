@@ -44,17 +44,27 @@ struct BlendFwdParams {
   int* n_contrib;
 };
 
+// Warp-uniform test: can splat record r0 = (mean, extent) reach this warp's 8x4 pixel block?
+__device__ __forceinline__ bool warp_block_hit(float4 r0, float wx0, float wy0) {
+  return r0.x + r0.z >= wx0 && r0.x - r0.z <= wx0 + 7.0f && r0.y + r0.w >= wy0 &&
+         r0.y - r0.w <= wy0 + 3.0f;
+}
+
 // Forward blend (csrc/forward/rasterize.cu:188-280): for each pixel, in depth order,
 // alpha = min(0.99, o * exp(power)), skipped when power > 0 or alpha < 1/255; colour
 // accumulates c * alpha * T and T *= 1 - alpha; the pixel stops after the Gaussian that
-// takes T below 1e-4. n_contrib counts Gaussians walked up to the last one applied.
+// takes T below 1e-4. n_contrib is the 1-based list position of the last Gaussian applied.
+// A warp skips splats whose extent box misses its pixel block (warp_block_hit): those fail
+// the opacity test at every pixel of the block, so the outputs are unchanged.
 static __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(BlendFwdParams p) {
   __shared__ float4 s_rec[2][3][kBlendBatch];
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   int px, py;
   tile_pixel(tile_x, tile_y, px, py);
+  const float wx0 = (float)(tile_x * kTileSide + (warp & 1) * 8);
+  const float wy0 = (float)(tile_y * kTileSide + (warp >> 1) * 4);
   const bool inside = px < p.W && py < p.H;
   const int2 range = p.ranges[blockIdx.x];
   const int K = range.y - range.x;
@@ -74,7 +84,7 @@ static __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(Ble
   };
 
   float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-  int contributor = 0, last = 0;
+  int last = 0;
   bool done = !inside;
   const float fpx = (float)px, fpy = (float)py;
   if (nbatches > 0) issue(0);
@@ -90,20 +100,21 @@ static __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(Ble
     const float4(*rec)[kBlendBatch] = s_rec[b & 1];
     if (!done) {
       for (int i = 0; i < n; ++i) {
-        ++contributor;
         const float4 r0 = rec[0][i];
+        if (!warp_block_hit(r0, wx0, wy0)) continue;
         const float4 r1 = rec[1][i];
         const float dx = fpx - r0.x, dy = fpy - r0.y;
-        const float power = splat_power(make_float3(r0.z, r0.w, r1.x), dx, dy);
+        const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
         if (power > 0.0f) continue;
-        const float alpha = fminf(0.99f, r1.y * __expf(power));
+        const float alpha = fminf(0.99f, r1.w * __expf(power));
         if (alpha < (1.0f / 255.0f)) continue;
+        const float4 r2 = rec[2][i];
         const float weight = alpha * T;
-        cr += r1.z * weight;
-        cg += r1.w * weight;
-        cb += rec[2][i].x * weight;
+        cr += r2.x * weight;
+        cg += r2.y * weight;
+        cb += r2.z * weight;
         T *= (1.0f - alpha);
-        last = contributor;
+        last = b * kBlendBatch + i + 1;
         if (T < 1e-4f) {
           done = true;
           break;
@@ -191,8 +202,9 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // Gaussians back to front from its n_contrib, recovering T before each one as
 // T / max(1 - alpha, 1e-4), and produces dL/d(mean, conic, colour, opacity). The tile
 // walk starts at the batch holding the tile's largest n_contrib instead of the list end.
-// Per Gaussian, the 256 pixel contributions are reduced per warp (warp_reduce9) and added
-// into a per-batch shared slot; after each batch the slot sums are converted from
+// Each warp starts at its own largest n_contrib and skips splats whose extent box misses its
+// pixel block (exact: they fail the opacity test there). Per Gaussian, the pixel
+// contributions are reduced per warp (warp_reduce9) and added into a per-batch shared slot; after each batch the slot sums are converted from
 // dL/dconic to dL/dSigma2 = -V G V (V the conic, G its symmetric gradient) and added to
 // the global gradients with one atomic per component.
 //
@@ -208,9 +220,11 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
   __shared__ float s_acc[kBlendBatch * kAccStride];
   __shared__ int s_max_last;
   const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   int px, py;
   tile_pixel(tile_x, tile_y, px, py);
+  const float wx0 = (float)(tile_x * kTileSide + (warp & 1) * 8);
+  const float wy0 = (float)(tile_y * kTileSide + (warp >> 1) * 4);
   const bool inside = px < p.W && py < p.H;
   const int pix = py * p.W + px;
   const int2 range = p.ranges[blockIdx.x];
@@ -228,8 +242,8 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
   if (tid == 0) s_max_last = 0;
   for (int k = tid; k < kBlendBatch * kAccStride; k += kBlendThreads) s_acc[k] = 0.0f;
   __syncthreads();
-  const int wmax = __reduce_max_sync(0xffffffffu, last);
-  if ((tid & 31) == 0 && wmax > 0) atomicMax(&s_max_last, wmax);
+  const int warp_last = __reduce_max_sync(0xffffffffu, last);  // this warp's replay length
+  if ((tid & 31) == 0 && warp_last > 0) atomicMax(&s_max_last, warp_last);
   __syncthreads();
   const int K_eff = s_max_last;  // list prefix that any pixel of this tile replays
   const int nbatches = (K_eff + kBlendBatch - 1) / kBlendBatch;
@@ -249,10 +263,10 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
         cp_async16(&dst[1][tid], src + 1);
         cp_async16(&dst[2][tid], src + 2);
       } else {
-        // out-of-range id: a record that never passes the opacity test and is not flushed
-        dst[0][tid] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        // out-of-range id: a record no warp touches and the flush skips
+        dst[0][tid] = make_float4(0.0f, 0.0f, -INFINITY, -INFINITY);
         dst[1][tid] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        dst[2][tid] = make_float4(0.0f, __int_as_float(-1), 0.0f, 0.0f);
+        dst[2][tid] = make_float4(0.0f, 0.0f, 0.0f, __int_as_float(-1));
       }
     }
     cp_async_commit();
@@ -271,25 +285,27 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
     __syncthreads();
     const int lo = batch_lo(b), hi = batch_hi(b);
     const float4(*rec)[kBlendBatch] = s_rec[b & 1];
-    for (int j = hi - 1; j >= lo; --j) {
+    for (int j = min(hi, warp_last) - 1; j >= lo; --j) {
       const int k = j - lo;  // slot in this batch
+      const float4 r0 = rec[0][k];
+      if (!warp_block_hit(r0, wx0, wy0)) continue;
       float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       bool active = false;
       if (j < last) {  // contributor j + 1 <= n_contrib
-        const float4 r0 = rec[0][k];
         const float4 r1 = rec[1][k];
         const float dx = fpx - r0.x, dy = fpy - r0.y;
-        const float cx = r0.z, cy = r0.w, cz = r1.x;
+        const float cx = r1.x, cy = r1.y, cz = r1.z;
         const float power = splat_power(make_float3(cx, cy, cz), dx, dy);
         if (power <= 0.0f) {
           const float G = __expf(power);
-          const float alpha_raw = r1.y * G;
+          const float alpha_raw = r1.w * G;
           const float alpha = fminf(0.99f, alpha_raw);
           if (alpha >= (1.0f / 255.0f)) {
             active = true;
+            const float4 r2 = rec[2][k];
             const float one_minus = 1.0f - alpha;
             const float T_before = T / fmaxf(one_minus, 1e-4f);
-            const float c0 = r1.z, c1 = r1.w, c2 = rec[2][k].x;
+            const float c0 = r2.x, c1 = r2.y, c2 = r2.z;
             const float wgt = alpha * T_before;
             v[5] = wgt * gr;
             v[6] = wgt * gg;
@@ -324,7 +340,7 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
     // flush this batch's slot sums to the global gradients
     if (tid < hi - lo) {
       float* acc = &s_acc[tid * kAccStride];
-      const int g = __float_as_int(rec[2][tid].y);
+      const int g = __float_as_int(rec[2][tid].w);
       bool any = false;
 #pragma unroll
       for (int q = 0; q < 9; ++q) any |= acc[q] != 0.0f;
@@ -336,7 +352,8 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
       } else if (any && g >= 0 && g < p.N) {
         atomicAdd(p.g_mean2d + 2 * g, acc[0]);
         atomicAdd(p.g_mean2d + 2 * g + 1, acc[1]);
-        const float vx = rec[0][tid].z, vy = rec[0][tid].w, vz = rec[1][tid].x;
+        const float4 r1 = rec[1][tid];
+        const float vx = r1.x, vy = r1.y, vz = r1.z;
         const float gx = acc[2], gy = 0.5f * acc[3], gz = acc[4];
         atomicAdd(p.g_cov2d + 3 * g,
                   -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz));

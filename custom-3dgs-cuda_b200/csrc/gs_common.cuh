@@ -85,6 +85,24 @@ __device__ __forceinline__ float3 conic_from_cov(float a, float b, float c) {
   return make_float3(c * det_inv, -b * det_inv, a * det_inv);
 }
 
+// Conservative half-extents (hx, hy) of the screen region where a splat can pass the blend's
+// opacity test, o * exp(-0.5 d^T Q d) >= 1/255, i.e. d^T Q d <= 2 ln(255 o): the axis-aligned
+// bounding box of that ellipse (half-widths sqrt(r^2 (Q^-1)_xx), sqrt(r^2 (Q^-1)_yy), with Q^-1
+// formed in double from the float conic) inflated by 1% in r^2 and 0.5 px. Pixels outside the
+// box fail the test for certain, so a warp whose pixels all lie outside may skip the splat
+// without changing any result. A splat that can never pass gets -inf; a conic whose inverse
+// cannot be formed gets +inf (never skipped).
+__device__ __forceinline__ float2 splat_extent(float3 conic, float opacity) {
+  const double r2_base = 2.0 * log(255.0 * (double)opacity);
+  if (!(opacity > 0.0f) || r2_base < -1e-3) return make_float2(-INFINITY, -INFINITY);
+  const double qx = conic.x, qy = conic.y, qz = conic.z;
+  const double det = qx * qz - qy * qy;
+  if (!(det > 0.0) || !(qx > 0.0) || !(qz > 0.0)) return make_float2(INFINITY, INFINITY);
+  const double r2 = fmax(r2_base, 0.0) * 1.01 + 1e-3;
+  const double hx = sqrt(r2 * qz / det) + 0.5, hy = sqrt(r2 * qx / det) + 0.5;
+  return make_float2((float)hx, (float)hy);
+}
+
 // Gaussian falloff exponent of a pixel offset (dx, dy) under a conic; the same expression
 // as csrc/forward/rasterize.cu:249-251.
 __device__ __forceinline__ float splat_power(float3 conic, float dx, float dy) {

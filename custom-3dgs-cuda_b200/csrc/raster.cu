@@ -21,9 +21,12 @@ __global__ void __launch_bounds__(256) build_records_kernel(int N, const float* 
   if (i >= N) return;
   const float a = cov2d[3 * i], b = cov2d[3 * i + 1], c = cov2d[3 * i + 2];
   const float3 conic = conic_from_cov(a, b, c);
-  records[3 * i + 0] = make_float4(mean2d[2 * i], mean2d[2 * i + 1], conic.x, conic.y);
-  records[3 * i + 1] = make_float4(conic.z, alpha[i], colors[3 * i], colors[3 * i + 1]);
-  records[3 * i + 2] = make_float4(colors[3 * i + 2], __int_as_float(i), 0.0f, 0.0f);
+  const float op = alpha[i];
+  const float2 ext = splat_extent(conic, op);
+  records[3 * i + 0] = make_float4(mean2d[2 * i], mean2d[2 * i + 1], ext.x, ext.y);
+  records[3 * i + 1] = make_float4(conic.x, conic.y, conic.z, op);
+  records[3 * i + 2] = make_float4(colors[3 * i], colors[3 * i + 1], colors[3 * i + 2],
+                                   __int_as_float(i));
 }
 
 static int tile_sort_passes(long long T) {

@@ -150,8 +150,8 @@ __global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianB
 #pragma unroll
     for (int k = 0; k < kShRestFloats; ++k) kj[k] = stage[lane * kShRestFloats + k];
     // dL/dconic -> dL/dSigma2 = -V G V with G's off-diagonal half of the packed sum
-    const float4 r0 = p.records[3 * i], r1 = p.records[3 * i + 1];
-    const float vx = r0.z, vy = r0.w, vz = r1.x;
+    const float4 r1 = p.records[3 * i + 1];
+    const float vx = r1.x, vy = r1.y, vz = r1.z;
     const float gx = a0.z, gy = 0.5f * a0.w, gz = a1.x;
     const float3 gcov = make_float3(-(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz),
                                     -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz),

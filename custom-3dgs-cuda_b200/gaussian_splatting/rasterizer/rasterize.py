@@ -78,7 +78,6 @@ class RasterizeFunction(t.autograd.Function):
         g_mu, g_q, g_s, g_alpha, g_albedo, g_kj, g_mean2d = render_backward(
             ctx.state, grad_output, mu, q, s, albedo, k_j, cam_rotation, cam_translation,
             cam_position, ctx.fx, ctx.fy, ctx.cx, ctx.cy)
-        ctx.state = None
         RasterizeFunction.last_mean2d_grad = g_mean2d
         return (g_mu, g_q, g_s, g_alpha.view_as(alpha), g_albedo, g_kj,
                 None, None, None, None, None, None, None, None)
