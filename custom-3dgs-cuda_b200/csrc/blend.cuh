@@ -1,18 +1,20 @@
 // Front-to-back alpha blending of 16x16 tiles and its backward.
 //
-// One CTA of 256 threads per tile, one pixel per thread; warp w covers the 8x4 pixel block
-// at ((w & 1) * 8, (w >> 1) * 4) of the tile, so small splats touch few warps. The tile's
-// depth-sorted Gaussians are consumed in batches of 256 blend records (48 bytes each)
-// gathered with cp.async into a double-buffered shared-memory ring: batch b + 1 is in
-// flight while batch b is blended.
+// One CTA per tile with 256 / kPix threads; each thread owns kPix pixels of one column,
+// 4 rows apart, so warp w covers the 8 x (4 kPix) pixel block at ((w & 1) * 8, (w >> 1) * 4 kPix)
+// of the tile. Pixels of a thread share each splat-record load, the warp's cull test and, in
+// the backward, one warp reduction. The tile's depth-sorted splats are consumed in batches of
+// 256 blend records (48 bytes each) gathered with cp.async into a double-buffered
+// shared-memory ring: batch b + 1 is in flight while batch b is blended.
 #pragma once
 
 #include "gs_common.cuh"
 
 namespace gs {
 
-constexpr int kBlendThreads = 256;
 constexpr int kBlendBatch = 256;
+constexpr int kBlendFwdPix = 2;  // pixels per thread of the forward blend
+constexpr int kBlendBwdPix = 2;  // pixels per thread of the backward blend
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -26,10 +28,27 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ void tile_pixel(int tile_x, int tile_y, int& px, int& py) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  px = tile_x * kTileSide + (warp & 1) * 8 + (lane & 7);
-  py = tile_y * kTileSide + (warp >> 1) * 4 + (lane >> 3);
+// Pixel block of this thread's warp and the column / first row of the thread's pixels.
+template <int kPix>
+struct BlendGeometry {
+  float wx0, wy0;  // warp block origin
+  int px, py0;     // thread column, first row; pixel q is at (px, py0 + 4 q)
+  __device__ __forceinline__ BlendGeometry(int tile_x, int tile_y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bx = tile_x * kTileSide + (warp & 1) * 8;
+    const int by = tile_y * kTileSide + (warp >> 1) * 4 * kPix;
+    wx0 = (float)bx;
+    wy0 = (float)by;
+    px = bx + (lane & 7);
+    py0 = by + (lane >> 3);
+  }
+};
+
+// Warp-uniform test: can splat record r0 = (mean, extent) reach the warp's pixel block?
+template <int kPix>
+__device__ __forceinline__ bool warp_block_hit(float4 r0, float wx0, float wy0) {
+  return r0.x + r0.z >= wx0 && r0.x - r0.z <= wx0 + 7.0f && r0.y + r0.w >= wy0 &&
+         r0.y - r0.w <= wy0 + (4.0f * kPix - 1.0f);
 }
 
 struct BlendFwdParams {
@@ -44,49 +63,55 @@ struct BlendFwdParams {
   int* n_contrib;
 };
 
-// Warp-uniform test: can splat record r0 = (mean, extent) reach this warp's 8x4 pixel block?
-__device__ __forceinline__ bool warp_block_hit(float4 r0, float wx0, float wy0) {
-  return r0.x + r0.z >= wx0 && r0.x - r0.z <= wx0 + 7.0f && r0.y + r0.w >= wy0 &&
-         r0.y - r0.w <= wy0 + 3.0f;
-}
-
 // Forward blend (csrc/forward/rasterize.cu:188-280): for each pixel, in depth order,
 // alpha = min(0.99, o * exp(power)), skipped when power > 0 or alpha < 1/255; colour
 // accumulates c * alpha * T and T *= 1 - alpha; the pixel stops after the Gaussian that
 // takes T below 1e-4. n_contrib is the 1-based list position of the last Gaussian applied.
 // A warp skips splats whose extent box misses its pixel block (warp_block_hit): those fail
 // the opacity test at every pixel of the block, so the outputs are unchanged.
-static __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(BlendFwdParams p) {
+template <int kPix>
+static __global__ void __launch_bounds__(kTilePixels / kPix)
+    blend_forward_kernel(BlendFwdParams p) {
+  constexpr int kThreads = kTilePixels / kPix;
   __shared__ float4 s_rec[2][3][kBlendBatch];
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  int px, py;
-  tile_pixel(tile_x, tile_y, px, py);
-  const float wx0 = (float)(tile_x * kTileSide + (warp & 1) * 8);
-  const float wy0 = (float)(tile_y * kTileSide + (warp >> 1) * 4);
-  const bool inside = px < p.W && py < p.H;
+  const int tid = threadIdx.x;
+  const BlendGeometry<kPix> geo(tile_x, tile_y);
   const int2 range = p.ranges[blockIdx.x];
   const int K = range.y - range.x;
   const int nbatches = (K + kBlendBatch - 1) / kBlendBatch;
 
+  static_assert(kBlendBatch % kThreads == 0, "each thread issues whole records");
   auto issue = [&](int b) {
-    const int j = b * kBlendBatch + tid;
-    if (j < K) {
-      const int g = p.sorted_ids[range.x + j];
-      const float4* src = p.records + 3 * (size_t)g;
-      float4(*dst)[kBlendBatch] = s_rec[b & 1];
-      cp_async16(&dst[0][tid], src);
-      cp_async16(&dst[1][tid], src + 1);
-      cp_async16(&dst[2][tid], src + 2);
+    float4(*dst)[kBlendBatch] = s_rec[b & 1];
+#pragma unroll
+    for (int r = 0; r < kBlendBatch / kThreads; ++r) {
+      const int slot = tid + r * kThreads;
+      const int j = b * kBlendBatch + slot;
+      if (j < K) {
+        const int g = p.sorted_ids[range.x + j];
+        const float4* src = p.records + 3 * (size_t)g;
+        cp_async16(&dst[0][slot], src);
+        cp_async16(&dst[1][slot], src + 1);
+        cp_async16(&dst[2][slot], src + 2);
+      }
     }
     cp_async_commit();
   };
 
-  float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-  int last = 0;
-  bool done = !inside;
-  const float fpx = (float)px, fpy = (float)py;
+  float T[kPix], cr[kPix], cg[kPix], cb[kPix], fpy[kPix];
+  int last[kPix];
+  bool done[kPix];
+  const float fpx = (float)geo.px;
+#pragma unroll
+  for (int q = 0; q < kPix; ++q) {
+    T[q] = 1.0f;
+    cr[q] = cg[q] = cb[q] = 0.0f;
+    last[q] = 0;
+    done[q] = !(geo.px < p.W && geo.py0 + 4 * q < p.H);
+    fpy[q] = (float)(geo.py0 + 4 * q);
+  }
   if (nbatches > 0) issue(0);
   for (int b = 0; b < nbatches; ++b) {
     if (b + 1 < nbatches) {
@@ -98,39 +123,44 @@ static __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(Ble
     __syncthreads();
     const int n = min(kBlendBatch, K - b * kBlendBatch);
     const float4(*rec)[kBlendBatch] = s_rec[b & 1];
-    if (!done) {
-      for (int i = 0; i < n; ++i) {
-        const float4 r0 = rec[0][i];
-        if (!warp_block_hit(r0, wx0, wy0)) continue;
-        const float4 r1 = rec[1][i];
-        const float dx = fpx - r0.x, dy = fpy - r0.y;
+    bool all_done = true;
+#pragma unroll
+    for (int q = 0; q < kPix; ++q) all_done = all_done && done[q];
+    for (int i = 0; i < n && !all_done; ++i) {
+      const float4 r0 = rec[0][i];
+      if (!warp_block_hit<kPix>(r0, geo.wx0, geo.wy0)) continue;
+      const float4 r1 = rec[1][i];
+      const float dx = fpx - r0.x;
+#pragma unroll
+      for (int q = 0; q < kPix; ++q) {
+        if (done[q]) continue;
+        const float dy = fpy[q] - r0.y;
         const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
         if (power > 0.0f) continue;
-        const float alpha = fminf(0.99f, r1.w * __expf(power));
+        const float alpha = fminf(0.99f, __fmul_rn(r1.w, __expf(power)));
         if (alpha < (1.0f / 255.0f)) continue;
-        const float4 r2 = rec[2][i];
-        const float weight = alpha * T;
-        cr += r2.x * weight;
-        cg += r2.y * weight;
-        cb += r2.z * weight;
-        T *= (1.0f - alpha);
-        last = b * kBlendBatch + i + 1;
-        if (T < 1e-4f) {
-          done = true;
-          break;
-        }
+        blend_step(alpha, rec[2][i], T[q], cr[q], cg[q], cb[q]);
+        last[q] = b * kBlendBatch + i + 1;
+        if (T[q] < 1e-4f) done[q] = true;
       }
+      all_done = true;
+#pragma unroll
+      for (int q = 0; q < kPix; ++q) all_done = all_done && done[q];
     }
-    if (__syncthreads_count(done) == kBlendThreads) break;
+    if (__syncthreads_count(all_done) == kThreads) break;
   }
   cp_async_wait<0>();
-  if (inside) {
-    const int pix = py * p.W + px;
-    p.img[3 * pix + 0] = cr;
-    p.img[3 * pix + 1] = cg;
-    p.img[3 * pix + 2] = cb;
-    p.final_T[pix] = T;
-    p.n_contrib[pix] = last;
+#pragma unroll
+  for (int q = 0; q < kPix; ++q) {
+    const int py = geo.py0 + 4 * q;
+    if (geo.px < p.W && py < p.H) {
+      const int pix = py * p.W + geo.px;
+      p.img[3 * pix + 0] = cr[q];
+      p.img[3 * pix + 1] = cg[q];
+      p.img[3 * pix + 2] = cb[q];
+      p.final_T[pix] = T[q];
+      p.n_contrib[pix] = last[q];
+    }
   }
 }
 
@@ -201,12 +231,11 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // Backward blend (csrc/backward/rasterize_backward.cu:60-235). Each pixel replays its
 // Gaussians back to front from its n_contrib, recovering T before each one as
 // T / max(1 - alpha, 1e-4), and produces dL/d(mean, conic, colour, opacity). The tile
-// walk starts at the batch holding the tile's largest n_contrib instead of the list end.
-// Each warp starts at its own largest n_contrib and skips splats whose extent box misses its
-// pixel block (exact: they fail the opacity test there). Per Gaussian, the pixel
-// contributions are reduced per warp (warp_reduce9) and added into a per-batch shared slot; after each batch the slot sums are converted from
-// dL/dconic to dL/dSigma2 = -V G V (V the conic, G its symmetric gradient) and added to
-// the global gradients with one atomic per component.
+// walk starts at the batch holding the tile's largest n_contrib instead of the list end;
+// each warp starts at its own largest n_contrib and skips splats whose extent box misses its
+// pixel block (exact: they fail the opacity test there). Per Gaussian, the contributions of a
+// thread's pixels are summed, reduced per warp (warp_reduce9) and added into a per-batch shared
+// slot; after each batch the slot sums are flushed to the global gradients.
 //
 // kFusedAccum selects the flush: false converts each tile's dL/dconic to dL/dSigma2 and adds
 // into the four reference-layout gradient arrays (9 scalar atomics, as the reference does);
@@ -214,35 +243,42 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 //   [0] = (dmean.x, dmean.y, dconic.x, dconic.y), [1] = (dconic.z, dopacity, dcol.r, dcol.g),
 //   [2] = (dcol.b, -, -, -), and the conversion happens once per Gaussian later
 //   (dL/dSigma2 is linear in dL/dconic for a fixed conic, so the sums commute with it).
-template <bool kFusedAccum>
-__global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdParams p) {
+template <bool kFusedAccum, int kPix>
+__global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(BlendBwdParams p) {
+  constexpr int kThreads = kTilePixels / kPix;
   __shared__ float4 s_rec[2][3][kBlendBatch];
   __shared__ float s_acc[kBlendBatch * kAccStride];
   __shared__ int s_max_last;
   const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  int px, py;
-  tile_pixel(tile_x, tile_y, px, py);
-  const float wx0 = (float)(tile_x * kTileSide + (warp & 1) * 8);
-  const float wy0 = (float)(tile_y * kTileSide + (warp >> 1) * 4);
-  const bool inside = px < p.W && py < p.H;
-  const int pix = py * p.W + px;
+  const int tid = threadIdx.x;
+  const BlendGeometry<kPix> geo(tile_x, tile_y);
   const int2 range = p.ranges[blockIdx.x];
   const int K = range.y - range.x;
 
-  float gr = 0.0f, gg = 0.0f, gb = 0.0f, T = 0.0f;
-  int last = 0;
-  if (inside) {
-    gr = p.grad_img[3 * pix];
-    gg = p.grad_img[3 * pix + 1];
-    gb = p.grad_img[3 * pix + 2];
-    T = p.final_T[pix];
-    last = min(p.n_contrib[pix], K);
+  float gr[kPix], gg[kPix], gb[kPix], T[kPix], ar[kPix], ag[kPix], ab[kPix], fpy[kPix];
+  int last[kPix];
+  int my_last = 0;
+#pragma unroll
+  for (int q = 0; q < kPix; ++q) {
+    const int py = geo.py0 + 4 * q;
+    gr[q] = gg[q] = gb[q] = T[q] = 0.0f;
+    ar[q] = ag[q] = ab[q] = 0.0f;
+    last[q] = 0;
+    fpy[q] = (float)py;
+    if (geo.px < p.W && py < p.H) {
+      const int pix = py * p.W + geo.px;
+      gr[q] = p.grad_img[3 * pix];
+      gg[q] = p.grad_img[3 * pix + 1];
+      gb[q] = p.grad_img[3 * pix + 2];
+      T[q] = p.final_T[pix];
+      last[q] = min(p.n_contrib[pix], K);
+    }
+    my_last = max(my_last, last[q]);
   }
   if (tid == 0) s_max_last = 0;
-  for (int k = tid; k < kBlendBatch * kAccStride; k += kBlendThreads) s_acc[k] = 0.0f;
+  for (int k = tid; k < kBlendBatch * kAccStride; k += kThreads) s_acc[k] = 0.0f;
   __syncthreads();
-  const int warp_last = __reduce_max_sync(0xffffffffu, last);  // this warp's replay length
+  const int warp_last = __reduce_max_sync(0xffffffffu, my_last);  // this warp's replay length
   if ((tid & 31) == 0 && warp_last > 0) atomicMax(&s_max_last, warp_last);
   __syncthreads();
   const int K_eff = s_max_last;  // list prefix that any pixel of this tile replays
@@ -251,29 +287,33 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
   // batch b covers list indices [lo(b), hi(b)) walking from the back
   auto batch_hi = [&](int b) { return K_eff - b * kBlendBatch; };
   auto batch_lo = [&](int b) { return max(0, K_eff - (b + 1) * kBlendBatch); };
+  static_assert(kBlendBatch % kThreads == 0, "each thread issues whole records");
   auto issue = [&](int b) {
     const int lo = batch_lo(b), hi = batch_hi(b);
-    const int j = lo + tid;
-    if (j < hi) {
-      int g = p.sorted_ids[range.x + j];
-      float4(*dst)[kBlendBatch] = s_rec[b & 1];
-      if (g >= 0 && g < p.N) {
-        const float4* src = p.records + 3 * (size_t)g;
-        cp_async16(&dst[0][tid], src);
-        cp_async16(&dst[1][tid], src + 1);
-        cp_async16(&dst[2][tid], src + 2);
-      } else {
-        // out-of-range id: a record no warp touches and the flush skips
-        dst[0][tid] = make_float4(0.0f, 0.0f, -INFINITY, -INFINITY);
-        dst[1][tid] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        dst[2][tid] = make_float4(0.0f, 0.0f, 0.0f, __int_as_float(-1));
+    float4(*dst)[kBlendBatch] = s_rec[b & 1];
+#pragma unroll
+    for (int r = 0; r < kBlendBatch / kThreads; ++r) {
+      const int slot = tid + r * kThreads;
+      const int j = lo + slot;
+      if (j < hi) {
+        const int g = p.sorted_ids[range.x + j];
+        if (g >= 0 && g < p.N) {
+          const float4* src = p.records + 3 * (size_t)g;
+          cp_async16(&dst[0][slot], src);
+          cp_async16(&dst[1][slot], src + 1);
+          cp_async16(&dst[2][slot], src + 2);
+        } else {
+          // out-of-range id: a record no warp touches and the flush skips
+          dst[0][slot] = make_float4(0.0f, 0.0f, -INFINITY, -INFINITY);
+          dst[1][slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          dst[2][slot] = make_float4(0.0f, 0.0f, 0.0f, __int_as_float(-1));
+        }
       }
     }
     cp_async_commit();
   };
 
-  float ar = 0.0f, ag = 0.0f, ab = 0.0f;  // colour of everything behind, front-weighted
-  const float fpx = (float)px, fpy = (float)py;
+  const float fpx = (float)geo.px;
   if (nbatches > 0) issue(0);
   for (int b = 0; b < nbatches; ++b) {
     if (b + 1 < nbatches) {
@@ -288,46 +328,49 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
     for (int j = min(hi, warp_last) - 1; j >= lo; --j) {
       const int k = j - lo;  // slot in this batch
       const float4 r0 = rec[0][k];
-      if (!warp_block_hit(r0, wx0, wy0)) continue;
+      if (!warp_block_hit<kPix>(r0, geo.wx0, geo.wy0)) continue;
       float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       bool active = false;
-      if (j < last) {  // contributor j + 1 <= n_contrib
-        const float4 r1 = rec[1][k];
-        const float dx = fpx - r0.x, dy = fpy - r0.y;
-        const float cx = r1.x, cy = r1.y, cz = r1.z;
+      const float4 r1 = rec[1][k];
+      const float cx = r1.x, cy = r1.y, cz = r1.z;
+      const float dx = fpx - r0.x;
+#pragma unroll
+      for (int q = 0; q < kPix; ++q) {
+        if (j >= last[q]) continue;  // contributor j + 1 > n_contrib of this pixel
+        const float dy = fpy[q] - r0.y;
         const float power = splat_power(make_float3(cx, cy, cz), dx, dy);
-        if (power <= 0.0f) {
-          const float G = __expf(power);
-          const float alpha_raw = r1.w * G;
-          const float alpha = fminf(0.99f, alpha_raw);
-          if (alpha >= (1.0f / 255.0f)) {
-            active = true;
-            const float4 r2 = rec[2][k];
-            const float one_minus = 1.0f - alpha;
-            const float T_before = T / fmaxf(one_minus, 1e-4f);
-            const float c0 = r2.x, c1 = r2.y, c2 = r2.z;
-            const float wgt = alpha * T_before;
-            v[5] = wgt * gr;
-            v[6] = wgt * gg;
-            v[7] = wgt * gb;
-            const float dL_dalpha =
-                ((c0 - ar) * gr + (c1 - ag) * gg + (c2 - ab) * gb) * T_before;
-            float dL_dpower = 0.0f;
-            if (alpha_raw < 0.99f) {
-              v[8] = G * dL_dalpha;
-              dL_dpower = alpha * dL_dalpha;
-            }
-            v[0] = dL_dpower * (cx * dx + cy * dy);
-            v[1] = dL_dpower * (cy * dx + cz * dy);
-            v[2] = -0.5f * dL_dpower * dx * dx;
-            v[3] = -dL_dpower * dx * dy;
-            v[4] = -0.5f * dL_dpower * dy * dy;
-            ar = alpha * c0 + one_minus * ar;
-            ag = alpha * c1 + one_minus * ag;
-            ab = alpha * c2 + one_minus * ab;
-            T = T_before;
-          }
+        if (power > 0.0f) continue;
+        const float G = __expf(power);
+        const float alpha_raw = r1.w * G;
+        const float alpha = fminf(0.99f, alpha_raw);
+        if (alpha < (1.0f / 255.0f)) continue;
+        active = true;
+        const float4 r2 = rec[2][k];
+        const float one_minus = 1.0f - alpha;
+        // approximate division (2 ulp): the recovered T drifts by a few 1e-6 over a
+        // pixel's replay, far inside the gradient tolerance
+        const float T_before = __fdividef(T[q], fmaxf(one_minus, 1e-4f));
+        const float c0 = r2.x, c1 = r2.y, c2 = r2.z;
+        const float wgt = alpha * T_before;
+        v[5] += wgt * gr[q];
+        v[6] += wgt * gg[q];
+        v[7] += wgt * gb[q];
+        const float dL_dalpha =
+            ((c0 - ar[q]) * gr[q] + (c1 - ag[q]) * gg[q] + (c2 - ab[q]) * gb[q]) * T_before;
+        float dL_dpower = 0.0f;
+        if (alpha_raw < 0.99f) {
+          v[8] += G * dL_dalpha;
+          dL_dpower = alpha * dL_dalpha;
         }
+        v[0] += dL_dpower * (cx * dx + cy * dy);
+        v[1] += dL_dpower * (cy * dx + cz * dy);
+        v[2] += -0.5f * dL_dpower * dx * dx;
+        v[3] += -dL_dpower * dx * dy;
+        v[4] += -0.5f * dL_dpower * dy * dy;
+        ar[q] = alpha * c0 + one_minus * ar[q];
+        ag[q] = alpha * c1 + one_minus * ag[q];
+        ab[q] = alpha * c2 + one_minus * ab[q];
+        T[q] = T_before;
       }
       if (__any_sync(0xffffffffu, active)) {
         float sum;
@@ -338,9 +381,9 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
     }
     __syncthreads();
     // flush this batch's slot sums to the global gradients
-    if (tid < hi - lo) {
-      float* acc = &s_acc[tid * kAccStride];
-      const int g = __float_as_int(rec[2][tid].w);
+    for (int t = tid; t < hi - lo; t += kThreads) {
+      float* acc = &s_acc[t * kAccStride];
+      const int g = __float_as_int(rec[2][t].w);
       bool any = false;
 #pragma unroll
       for (int q = 0; q < 9; ++q) any |= acc[q] != 0.0f;
@@ -352,15 +395,13 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(BlendBwdP
       } else if (any && g >= 0 && g < p.N) {
         atomicAdd(p.g_mean2d + 2 * g, acc[0]);
         atomicAdd(p.g_mean2d + 2 * g + 1, acc[1]);
-        const float4 r1 = rec[1][tid];
+        const float4 r1 = rec[1][t];
         const float vx = r1.x, vy = r1.y, vz = r1.z;
         const float gx = acc[2], gy = 0.5f * acc[3], gz = acc[4];
-        atomicAdd(p.g_cov2d + 3 * g,
-                  -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz));
+        atomicAdd(p.g_cov2d + 3 * g, -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz));
         atomicAdd(p.g_cov2d + 3 * g + 1,
                   -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz));
-        atomicAdd(p.g_cov2d + 3 * g + 2,
-                  -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz));
+        atomicAdd(p.g_cov2d + 3 * g + 2, -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz));
         atomicAdd(p.g_colors + 3 * g, acc[5]);
         atomicAdd(p.g_colors + 3 * g + 1, acc[6]);
         atomicAdd(p.g_colors + 3 * g + 2, acc[7]);

@@ -6,7 +6,7 @@
 #include <exception>
 #include <string>
 
-#include "../../include/gs3d_b200.h"
+#include "gs3d_b200.h"
 
 namespace gs {
 

@@ -52,18 +52,25 @@ struct TileRect {
   int x0, y0, x1, y1;
 };
 
+// Written with explicit round-to-nearest intrinsics in the form nvcc gives the reference's
+// source under its default --fmad=true (a * c - b * b -> fma(a, c, -(b * b)), and so on), so the
+// rounding cannot change with the surrounding code.
+__device__ __forceinline__ float cov_det(float a, float b, float c) {
+  return __fmaf_rn(a, c, -__fmul_rn(b, b));
+}
+
 __device__ __forceinline__ bool splat_tile_rect(float2 mean, float a, float b, float c,
                                                 int width, int height, int tiles_x,
                                                 int tiles_y, TileRect& r) {
-  float det = a * c - b * b;
+  const float det = cov_det(a, b, c);
   if (det <= 0.0f) return false;
-  float mid = 0.5f * (a + c);
-  float lambda_max = mid + sqrtf(fmaxf(0.1f, mid * mid - det));
-  float radius = ceilf(3.0f * sqrtf(lambda_max));
-  int min_x = max(0, (int)floorf(mean.x - radius));
-  int max_x = min(width, (int)ceilf(mean.x + radius));
-  int min_y = max(0, (int)floorf(mean.y - radius));
-  int max_y = min(height, (int)ceilf(mean.y + radius));
+  const float mid = __fmul_rn(0.5f, __fadd_rn(a, c));
+  const float lambda_max = __fadd_rn(mid, __fsqrt_rn(fmaxf(0.1f, __fmaf_rn(mid, mid, -det))));
+  const float radius = ceilf(__fmul_rn(3.0f, __fsqrt_rn(lambda_max)));
+  int min_x = max(0, (int)floorf(__fsub_rn(mean.x, radius)));
+  int max_x = min(width, (int)ceilf(__fadd_rn(mean.x, radius)));
+  int min_y = max(0, (int)floorf(__fsub_rn(mean.y, radius)));
+  int max_y = min(height, (int)ceilf(__fadd_rn(mean.y, radius)));
   int tx0 = min_x / kTileSide, tx1 = (max_x + kTileSide - 1) / kTileSide;
   int ty0 = min_y / kTileSide, ty1 = (max_y + kTileSide - 1) / kTileSide;
   r.x0 = max(0, min(tiles_x, tx0));
@@ -80,9 +87,9 @@ __device__ __forceinline__ int rect_count(const TileRect& r) {
 // Conic (inverse 2D covariance) with the reference's guard det <= 0 -> 0
 // (csrc/forward/rasterize.cu:224-232).
 __device__ __forceinline__ float3 conic_from_cov(float a, float b, float c) {
-  float det = a * c - b * b;
-  float det_inv = (det > 0.0f) ? (1.0f / det) : 0.0f;
-  return make_float3(c * det_inv, -b * det_inv, a * det_inv);
+  const float det = cov_det(a, b, c);
+  const float det_inv = (det > 0.0f) ? __fdiv_rn(1.0f, det) : 0.0f;
+  return make_float3(__fmul_rn(c, det_inv), __fmul_rn(-b, det_inv), __fmul_rn(a, det_inv));
 }
 
 // Conservative half-extents (hx, hy) of the screen region where a splat can pass the blend's
@@ -103,10 +110,25 @@ __device__ __forceinline__ float2 splat_extent(float3 conic, float opacity) {
   return make_float2((float)hx, (float)hy);
 }
 
-// Gaussian falloff exponent of a pixel offset (dx, dy) under a conic; the same expression
-// as csrc/forward/rasterize.cu:249-251.
+// Gaussian falloff exponent of a pixel offset (dx, dy) under a conic:
+// -0.5 (q.x dx dx + 2 q.y dx dy + q.z dy dy) (csrc/forward/rasterize.cu:249-251), evaluated as
+// nvcc contracts that source: -0.5 * fma(q.z dy, dy, fma(q.x dx, dx, ((2 q.y) dx) dy)).
 __device__ __forceinline__ float splat_power(float3 conic, float dx, float dy) {
-  return -0.5f * (conic.x * dx * dx + 2.0f * conic.y * dx * dy + conic.z * dy * dy);
+  const float cross = __fmul_rn(__fmul_rn(__fmul_rn(2.0f, conic.y), dx), dy);
+  const float s1 = __fmaf_rn(__fmul_rn(conic.x, dx), dx, cross);
+  const float s = __fmaf_rn(__fmul_rn(conic.z, dy), dy, s1);
+  return __fmul_rn(-0.5f, s);
+}
+
+// One front-to-back blend step of a pixel (csrc/forward/rasterize.cu:260-264): the colour gains
+// c * (alpha T) and T becomes T (1 - alpha), with nvcc's contraction of the reference source.
+__device__ __forceinline__ void blend_step(float alpha, float4 col, float& T, float& r,
+                                           float& g, float& b) {
+  const float weight = __fmul_rn(alpha, T);
+  r = __fmaf_rn(col.x, weight, r);
+  g = __fmaf_rn(col.y, weight, g);
+  b = __fmaf_rn(col.z, weight, b);
+  T = __fmul_rn(T, __fsub_rn(1.0f, alpha));
 }
 
 // ---------------------------------------------------------------------------------------

@@ -206,7 +206,8 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
   fp.img = img;
   fp.final_T = final_T;
   fp.n_contrib = n_contrib;
-  blend_forward_kernel<<<(unsigned)L.T, kBlendThreads, 0, stream>>>(fp);
+  blend_forward_kernel<kBlendFwdPix>
+      <<<(unsigned)L.T, kTilePixels / kBlendFwdPix, 0, stream>>>(fp);
   GS_CHECK_LAUNCH();
   mark_stage(6, stream);
   return GS_OK;
@@ -318,7 +319,8 @@ extern "C" int gs_rasterize_backward(int N, int H, int W, const float* grad_img,
   bp.g_colors = g_colors;
   bp.g_alpha = g_alpha;
   bp.g_accum = nullptr;
-  blend_backward_kernel<false><<<(unsigned)(tiles_x * tiles_y), kBlendThreads, 0, st>>>(bp);
+  blend_backward_kernel<false, kBlendBwdPix>
+      <<<(unsigned)(tiles_x * tiles_y), kTilePixels / kBlendBwdPix, 0, st>>>(bp);
   GS_CHECK_LAUNCH();
   return GS_OK;
   GS_API_END();

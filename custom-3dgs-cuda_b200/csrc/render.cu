@@ -324,7 +324,8 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
   bp.n_contrib = n_contrib;
   bp.g_mean2d = bp.g_cov2d = bp.g_colors = bp.g_alpha = nullptr;
   bp.g_accum = accum;
-  blend_backward_kernel<true><<<(unsigned)L.T, kBlendThreads, 0, st>>>(bp);
+  blend_backward_kernel<true, kBlendBwdPix>
+      <<<(unsigned)L.T, kTilePixels / kBlendBwdPix, 0, st>>>(bp);
   GS_CHECK_LAUNCH();
   mark_stage(8, st);
   GaussianBwdParams gp;

@@ -7,10 +7,13 @@ if the shared library is missing or lacks a symbol, importing the package raises
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import c_float, c_int, c_longlong, c_size_t, c_uint, c_void_p, POINTER
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libgs3d_b200.so"
+# The library built in-tree by build.py; GS3D_B200_LIB may point at another build of it.
+LIB_PATH = Path(os.environ.get("GS3D_B200_LIB",
+                               Path(__file__).resolve().parent / "libgs3d_b200.so"))
 
 GS_OK = 0
 GS_ERR_INVALID_ARG = 1
