@@ -108,6 +108,10 @@ struct GaussianBwdParams {
   float fx, fy, cx, cy;
   float *g_mu, *g_q, *g_s, *g_opacity, *g_albedo, *g_k_j, *g_mean2d;
   int accumulate;
+  // densification statistics (optional): per Gaussian, n = |dL/dmean2d * (sx, sy)|; where
+  // n > 0: norm_sum += n, count += 1; norm_max = max(norm_max, n)
+  float *stat_norm_sum, *stat_count, *stat_max;
+  float stat_sx, stat_sy;
 };
 
 template <int F>
@@ -188,6 +192,15 @@ __global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianB
     if (p.g_mean2d) {
       put(p.g_mean2d + 2 * i, gmean.x, acc);
       put(p.g_mean2d + 2 * i + 1, gmean.y, acc);
+    }
+    if (p.stat_norm_sum) {
+      const float nx = gmean.x * p.stat_sx, ny = gmean.y * p.stat_sy;
+      const float n = sqrtf(nx * nx + ny * ny);
+      if (n > 0.0f) {
+        p.stat_norm_sum[i] += n;
+        p.stat_count[i] += 1.0f;
+        p.stat_max[i] = fmaxf(p.stat_max[i], n);
+      }
     }
   } else if (valid && !acc) {
     for (int k = 0; k < 3; ++k) p.g_mu[3 * i + k] = 0.f;
@@ -293,7 +306,9 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
                                   const float* final_T, const int* n_contrib, void* workspace,
                                   size_t workspace_bytes, float* g_mu, float* g_q, float* g_s,
                                   float* g_opacity, float* g_albedo, float* g_k_j,
-                                  float* g_mean2d, int accumulate, void* stream) {
+                                  float* g_mean2d, int accumulate, float* stat_norm_sum,
+                                  float* stat_count, float* stat_max, float stat_scale_x,
+                                  float stat_scale_y, void* stream) {
   GS_API_BEGIN();
   GS_REQUIRE(N >= 0, "N must be non-negative");
   GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
@@ -352,6 +367,14 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
   gp.g_k_j = g_k_j;
   gp.g_mean2d = g_mean2d;
   gp.accumulate = accumulate;
+  GS_REQUIRE((stat_norm_sum == nullptr) == (stat_count == nullptr) &&
+                 (stat_count == nullptr) == (stat_max == nullptr),
+             "the three statistics buffers go together");
+  gp.stat_norm_sum = stat_norm_sum;
+  gp.stat_count = stat_count;
+  gp.stat_max = stat_max;
+  gp.stat_sx = stat_scale_x;
+  gp.stat_sy = stat_scale_y;
   GS_CUDA(cudaFuncSetAttribute(render_gaussian_backward_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)kPreprocessSmem));

@@ -69,9 +69,11 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
 
 
 def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, cam_pos, fx, fy,
-                    cx, cy, want_mean2d_grad: bool = True, out=None):
+                    cx, cy, want_mean2d_grad: bool = True, out=None, stats=None):
     """Gradients (mu, q, s, opacity[N], albedo, k_j, mean2d or None). With `out` (a tuple of
-    the first six buffers) the gradients are added into those buffers instead."""
+    the first six buffers) the gradients are added into those buffers instead. `stats` =
+    (norm_sum[N], count[N], norm_max[N], scale_x, scale_y) updates the densification
+    statistics in the same pass."""
     N = int(mu.shape[0])
     dev = mu.device
     f32 = dict(device=dev, dtype=torch.float32)
@@ -91,5 +93,8 @@ def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, c
             float(cx), float(cy), state.workspace.data_ptr(), state.capacity,
             state.sorted_ids.data_ptr(), _ptr(state.tile_ranges), _ptr(state.final_T),
             _ptr(state.n_contrib), ws.data_ptr(), ws_bytes, *(_ptr(o) for o in out),
-            _ptr(g_mean2d), 1 if accumulate else 0, _stream(dev)))
+            _ptr(g_mean2d), 1 if accumulate else 0,
+            *((_ptr(stats[0]), _ptr(stats[1]), _ptr(stats[2]), float(stats[3]), float(stats[4]))
+              if stats is not None else (None, None, None, 0.0, 0.0)),
+            _stream(dev)))
     return (*out, g_mean2d)

@@ -54,3 +54,43 @@ class FusedL1SSIM(torch.autograd.Function):
 def l1_ssim_loss(img: torch.Tensor, target: torch.Tensor,
                  lambda_dssim: float = LAMBDA_DSSIM) -> torch.Tensor:
     return FusedL1SSIM.apply(img, target, lambda_dssim)
+
+
+class _OneCache:
+    """A device scalar 1.0 per device (the upstream gradient of a loss used directly)."""
+
+    def __init__(self) -> None:
+        self._ones: dict = {}
+
+    def get(self, dev) -> torch.Tensor:
+        t = self._ones.get(dev)
+        if t is None:
+            t = self._ones[dev] = torch.ones((), device=dev, dtype=torch.float32)
+        return t
+
+
+_one = _OneCache()
+
+
+def l1_ssim_value_and_grad(img: torch.Tensor, target: torch.Tensor,
+                           lambda_dssim: float = LAMBDA_DSSIM,
+                           grad_out: torch.Tensor | None = None):
+    """(loss, dloss/dimg) in two kernel launches, outside autograd; [H, W, 3] fp32 CUDA."""
+    img = img.contiguous()
+    target = target.contiguous()
+    H, W = int(img.shape[0]), int(img.shape[1])
+    dev = img.device
+    ws_bytes = _lib.lib.gs_l1_ssim_workspace_size(H, W)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    loss = torch.empty((), device=dev, dtype=torch.float32)
+    grad = torch.empty_like(img) if grad_out is None else grad_out
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib.gs_l1_ssim_forward(H, W, img.data_ptr(), target.data_ptr(),
+                                               float(lambda_dssim), ws.data_ptr(), ws_bytes,
+                                               loss.data_ptr(), None, stream))
+        _lib.check(_lib.lib.gs_l1_ssim_backward(H, W, img.data_ptr(), target.data_ptr(),
+                                                float(lambda_dssim), ws.data_ptr(), ws_bytes,
+                                                _one.get(dev).data_ptr(), grad.data_ptr(),
+                                                stream))
+    return loss, grad

@@ -124,10 +124,18 @@ def reduce_step(fg: FlatGrads, batch: int, world: int, group=None) -> None:
 
 
 class Trainer:
-    """Parameters, optimizer and flat gradient bucket of one rank."""
+    """Parameters, optimizer and flat gradient bucket of one rank.
+
+    mode "direct" (default) calls the fused render and loss kernels without autograd: each
+    view's parameter gradients are added straight into the flat bucket, the densification
+    statistics are updated inside the per-Gaussian backward kernel and the opacity gradient is
+    taken through the sigmoid once per step. mode "autograd" runs the same step through
+    `gaussian_splatting.rasterizer.rasterize` (the drop-in RasterizeFunction) and
+    loss.backward(), as the reference trainer does.
+    """
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
-                 fused_adam: bool = True, fused_loss: bool = True):
+                 fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct"):
         from gaussian_splatting.scene.gaussian import gaussian
 
         self.device = device
@@ -147,8 +155,55 @@ class Trainer:
         self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15, **kw)
         self.fg = FlatGrads(self.params, scene.N)
         self.fused_loss = fused_loss and device.type == "cuda"
+        if mode not in ("direct", "autograd"):
+            raise ValueError(f"unknown trainer mode {mode!r}")
+        self.mode = mode
+        self.cam_positions = [(-torch.matmul(v["R"].T, v["T"])).reshape(3).contiguous()
+                              for v in self.views]
+        self.g_opacity = torch.zeros(scene.N, device=device, dtype=torch.float32)
 
     def step(self, targets=None, before_view=None) -> torch.Tensor:
+        if self.mode == "direct":
+            return self._step_direct(targets, before_view)
+        return self._step_autograd(targets, before_view)
+
+    def _step_direct(self, targets=None, before_view=None) -> torch.Tensor:
+        """One step with the fused kernels called directly (see the class docstring)."""
+        from custom_rasterizer_cuda.render import render_backward, render_forward
+        from gs3d_b200.loss import l1_ssim_value_and_grad
+
+        targets = self.targets if targets is None else targets
+        g = self.gaussians
+        fg = self.fg
+        fg.zero()
+        fg.rebind(self.params)
+        self.g_opacity.zero_()
+        with torch.no_grad():
+            mu, q, s, A, kj = g.mu.detach(), g.q.detach(), g.s.detach(), g.A.detach(), g.k_j.detach()
+            opacity = torch.sigmoid(g.alpha.detach()).reshape(-1)
+            out = (g.mu.grad, g.q.grad, g.s.grad, self.g_opacity, g.A.grad, g.k_j.grad)
+            total = torch.zeros((), device=self.device)
+            for vi in self.plan.views():
+                v = self.views[vi]
+                cam = self.cam_positions[vi]
+                if before_view is not None:
+                    before_view(vi)
+                img, _, st = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
+                                            v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
+                                            v["width"])
+                loss, gimg = l1_ssim_value_and_grad(img, targets[vi], LAMBDA_DSSIM)
+                render_backward(st, gimg, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
+                                v["cx"], v["cy"], want_mean2d_grad=False, out=out,
+                                stats=(fg.grad_norm_sum, fg.grad_count, fg.max_grad,
+                                       v["width"] / 2.0, v["height"] / 2.0))
+                total += loss
+            # d loss / d logit = d loss / d opacity * sigmoid'(logit), once per step
+            g.alpha.grad.view(-1).addcmul_(self.g_opacity, opacity * (1.0 - opacity))
+        reduce_step(fg, len(self.views), self.world, self.group)
+        self.opt.step()
+        return total
+
+    def _step_autograd(self, targets=None, before_view=None) -> torch.Tensor:
         """One training step over this rank's share of the batch; returns the summed loss of
         the local views (a 0-d tensor on the device). `before_view(vi)`, if given, is called
         before view vi is rendered (the benchmark installs its stage events there)."""

@@ -151,7 +151,10 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
  * blend records from it.
  * gs_render_backward: gradients of every parameter (g_opacity w.r.t. the post-sigmoid
  * opacity) and, when g_mean2d is non-NULL, dL/dmean2d. With accumulate = 0 the outputs are
- * overwritten; otherwise the gradients are added to them.
+ * overwritten; otherwise the gradients are added to them. When the three stat_* buffers [N] are
+ * given, the reference trainer's densification statistics are updated in the same pass
+ * (gaussian_splatting/utils/adc.py:58-87): n = |dL/dmean2d * (stat_scale_x, stat_scale_y)|,
+ * and where n > 0, stat_norm_sum += n, stat_count += 1, stat_max = max(stat_max, n).
  */
 GS_API size_t gs_render_workspace_size(int N, int H, int W, long long pair_capacity);
 GS_API int gs_render_forward(int N, int H, int W, const float* mu, const float* q, const float* s,
@@ -172,7 +175,9 @@ GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const 
                               const float* final_T, const int* n_contrib, void* workspace,
                               size_t workspace_bytes, float* g_mu, float* g_q, float* g_s,
                               float* g_opacity, float* g_albedo, float* g_k_j, float* g_mean2d,
-                              int accumulate, void* stream);
+                              int accumulate, float* stat_norm_sum, float* stat_count,
+                              float* stat_max, float stat_scale_x, float stat_scale_y,
+                              void* stream);
 
 /*
  * Fused photometric loss of the training step (no counterpart in the reference's extension;

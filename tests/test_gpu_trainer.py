@@ -1,0 +1,56 @@
+"""The config-4 training step: the direct mode (fused kernels called without autograd, gradients
+accumulated into the flat bucket, statistics fused into the backward kernel) produces the same
+bucket as the autograd mode through RasterizeFunction and loss.backward(); Adam then moves the
+parameters identically."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from test_gpu_parity import assert_grad_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _small_setup():
+    from gs3d_b200 import scenes
+
+    sc = scenes.config2(7, n=60_000)
+    views = [scenes.pinhole(tuple(float(x) for x in e), 480, 270, 375.0)
+             for e in ((0.0, 0.0, 8.0), (5.0, 2.0, 6.0), (-6.0, -1.0, 5.0))]
+    g = torch.Generator("cpu").manual_seed(9)
+    targets = [torch.rand(270, 480, 3, generator=g) for _ in views]
+    return sc, views, targets
+
+
+def test_direct_and_autograd_steps_agree(cuda_device):
+    from gs3d_b200.train_step import Trainer
+
+    sc, views, targets = _small_setup()
+    tg = [t.to(cuda_device) for t in targets]
+    buckets = {}
+    for mode in ("direct", "autograd"):
+        tr = Trainer(sc, views, tg, cuda_device, mode=mode)
+        tr.opt.step = lambda: None  # compare the reduced bucket before any update
+        loss = tr.step()
+        torch.cuda.synchronize()
+        buckets[mode] = (float(loss), tr.fg.buffer.cpu().numpy().copy(),
+                         tr.fg.max_grad.cpu().numpy().copy(), tr.fg.n_param)
+    (l_d, b_d, m_d, n_param), (l_a, b_a, m_a, _) = buckets["direct"], buckets["autograd"]
+    assert abs(l_d - l_a) <= 1e-6 * abs(l_a)
+    assert_grad_close(b_d[:n_param], b_a[:n_param], "parameter gradients")
+    assert_grad_close(b_d[n_param:], b_a[n_param:], "densification sums")
+    assert_grad_close(m_d, m_a, "max screen gradient")
+
+
+def test_direct_step_trains(cuda_device):
+    """Three direct steps lower the loss on a fixed batch."""
+    from gs3d_b200.train_step import Trainer
+
+    sc, views, targets = _small_setup()
+    tr = Trainer(sc, views, [t.to(cuda_device) for t in targets], cuda_device)
+    losses = [float(tr.step()) for _ in range(4)]
+    assert losses[-1] < losses[0]
+    assert all(np.isfinite(losses))
