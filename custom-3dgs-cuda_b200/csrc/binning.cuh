@@ -48,8 +48,6 @@ struct BinParams {
   float4* records;
   unsigned* depth_keys;
   unsigned* depth_vals;
-  unsigned* status;             // look-back words, one per tile of kBinThreads Gaussians
-  unsigned* ticket;
   unsigned* done_counter;
   unsigned* depth_hist;         // [4][256]
   unsigned long long* pair_acc; // running pair total
@@ -83,40 +81,28 @@ __device__ __forceinline__ unsigned bin_gaussian(const BinParams& p, int i, floa
   return count;
 }
 
-// Block part of binning, called by all kBinThreads threads of a CTA that holds binning tile
-// `tile` (Gaussians [tile * kBinThreads, ...)): order-preserving compaction of the visible
-// Gaussians into the depth-sort input (decoupled look-back), the digit histograms of the four
-// depth passes, the running pair total and, in the last CTA to finish, M and N_visible.
+// Block part of binning, called by all kBinThreads threads of a CTA that holds Gaussians
+// [tile * kBinThreads, ...): the depth-sort input for every Gaussian (key = depth bits, or
+// 0xffffffff for a splat that covers no tile; value = index), the digit histograms of the four
+// depth passes, the running pair total and, in the last CTA to finish, M. Sorting all N keeps
+// the order the reference's stable 64-bit sort gives: splats without pairs are skipped by the
+// duplication, and ties on the key keep index order whatever their value.
 __device__ __forceinline__ void bin_block(const BinParams& p, int tile, int i, unsigned count,
                                           unsigned depth_bits, unsigned* s_scan,
-                                          unsigned (*s_hist)[256], unsigned& s_prefix,
-                                          bool& s_last) {
+                                          unsigned (*s_hist)[256], bool& s_last) {
   const int tid = threadIdx.x;
-  const unsigned visible = count > 0 ? 1u : 0u;
-  unsigned n_vis_tile;
-  const unsigned excl = block_exclusive_scan(visible, s_scan, &n_vis_tile);
-  if (tid == 0)
-    st_relaxed(p.status + tile, (tile == 0 ? kFlagPrefix : kFlagAggregate) | n_vis_tile);
-  if (tid < 32) {
-    unsigned prefix = 0;
-    if (tile > 0) prefix = lookback_warp(p.status, tile);
-    if (tid == 0) {
-      if (tile > 0) st_relaxed(p.status + tile, kFlagPrefix | (prefix + n_vis_tile));
-      s_prefix = prefix;
-    }
+  if (i < p.N) {
+    const unsigned key = count > 0 ? depth_bits : 0xffffffffu;
+    if (count == 0) p.rects[i] = make_uint2(0u, 0u);
+    p.depth_keys[i] = key;
+    p.depth_vals[i] = (unsigned)i;
+    atomicAdd(&s_hist[0][key & 255u], 1u);
+    atomicAdd(&s_hist[1][(key >> 8) & 255u], 1u);
+    atomicAdd(&s_hist[2][(key >> 16) & 255u], 1u);
+    atomicAdd(&s_hist[3][key >> 24], 1u);
   }
   unsigned tile_pairs;
-  block_exclusive_scan(count, s_scan, &tile_pairs);  // also orders s_prefix
-  if (visible && s_prefix + excl < (unsigned)p.N) {
-    const unsigned pos = s_prefix + excl;
-    p.depth_keys[pos] = depth_bits;
-    p.depth_vals[pos] = (unsigned)i;
-    atomicAdd(&s_hist[0][depth_bits & 255u], 1u);
-    atomicAdd(&s_hist[1][(depth_bits >> 8) & 255u], 1u);
-    atomicAdd(&s_hist[2][(depth_bits >> 16) & 255u], 1u);
-    atomicAdd(&s_hist[3][depth_bits >> 24], 1u);
-  }
-  __syncthreads();
+  block_exclusive_scan(count, s_scan, &tile_pairs);  // also orders the histogram updates
   for (int k = tid; k < 4 * 256; k += kBinThreads) {
     const unsigned h = (&s_hist[0][0])[k];
     if (h) atomicAdd(p.depth_hist + k, h);
@@ -124,31 +110,29 @@ __device__ __forceinline__ void bin_block(const BinParams& p, int tile, int i, u
   const int num_tiles = (p.N + kBinThreads - 1) / kBinThreads;
   if (tid == 0) {
     if (tile_pairs) atomicAdd(p.pair_acc, (unsigned long long)tile_pairs);
-    if (tile == num_tiles - 1) *p.n_visible = (int)(s_prefix + n_vis_tile);
     __threadfence();
     s_last = atomicAdd(p.done_counter, 1u) == (unsigned)(num_tiles - 1);
   }
   __syncthreads();
   if (s_last && tid == 0) {
-    // every other tile's pair total is visible after its fence + done_counter increment
+    // every other CTA's pair total is visible after its fence + done_counter increment
     __threadfence();
     const unsigned long long m = atomicAdd(p.pair_acc, 0ull);
     const unsigned long long clamped = m > 0x7fffffffull ? 0x7fffffffull : m;
     *p.pair_count = (int)clamped;
+    *p.n_visible = p.N;
     if (m > 0x7fffffffull) raise_device_error(kErrCapacity);
   }
 }
 
 static __global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinParams p) {
-  __shared__ unsigned s_tile, s_prefix;
   __shared__ unsigned s_scan[33];
   __shared__ unsigned s_hist[4][256];
   __shared__ bool s_last;
   const int tid = threadIdx.x;
-  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
   for (int i = tid; i < 4 * 256; i += kBinThreads) (&s_hist[0][0])[i] = 0u;
   __syncthreads();
-  const int tile = (int)s_tile;
+  const int tile = (int)blockIdx.x;
   const int i = tile * kBinThreads + tid;
   unsigned count = 0, depth_bits = 0;
   if (i < p.N) {
@@ -164,7 +148,7 @@ static __global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinPara
                            depth_bits);
     }
   }
-  bin_block(p, tile, i, count, depth_bits, s_scan, s_hist, s_prefix, s_last);
+  bin_block(p, tile, i, count, depth_bits, s_scan, s_hist, s_last);
 }
 
 struct DupParams {
@@ -173,7 +157,7 @@ struct DupParams {
   const int* n_visible;
   const int* pair_count;
   long long pair_capacity;
-  const unsigned* sorted_gids;  // depth-sorted visible Gaussians
+  const unsigned* sorted_gids;  // depth-sorted Gaussians
   const uint2* rects;
   unsigned* status;
   unsigned* ticket;

@@ -54,7 +54,6 @@ RasterLayout make_raster_layout(int N, int W, int H, long long capacity) {
   L.header = take(sizeof(RasterHeader));
   L.depth_hist = take(4 * 256 * sizeof(unsigned));
   L.tile_hist = take(4 * 256 * sizeof(unsigned));
-  L.status_bin = take(nb * sizeof(unsigned));
   L.status_dup = take(nb * sizeof(unsigned));
   L.status_depth = take(4 * nd * 256 * sizeof(unsigned));
   L.status_tile = take((size_t)std::max(L.tile_passes, 1) * nt * 256 * sizeof(unsigned));
@@ -105,8 +104,6 @@ void fill_bin_params(BinParams& bp, const RasterLayout& L, char* ws, int N, int 
   bp.records = reinterpret_cast<float4*>(ws + L.records);
   bp.depth_keys = reinterpret_cast<unsigned*>(ws + L.depth_keys[0]);
   bp.depth_vals = reinterpret_cast<unsigned*>(ws + L.depth_vals[0]);
-  bp.status = reinterpret_cast<unsigned*>(ws + L.status_bin);
-  bp.ticket = &hdr->ticket_bin;
   bp.done_counter = &hdr->done_bin;
   bp.depth_hist = reinterpret_cast<unsigned*>(ws + L.depth_hist);
   bp.pair_acc = &hdr->pair_acc;

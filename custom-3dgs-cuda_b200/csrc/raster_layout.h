@@ -9,7 +9,7 @@ namespace gs {
 
 struct RasterHeader {
   unsigned long long pair_acc;  // running total of (tile, Gaussian) pairs
-  unsigned ticket_bin, done_bin, ticket_dup;
+  unsigned done_bin, ticket_dup;
   unsigned ticket_depth[4];
   unsigned ticket_tile[4];
   int n_visible;   // Gaussians with at least one tile
@@ -19,7 +19,7 @@ struct RasterHeader {
 struct RasterLayout {
   int tiles_x = 0, tiles_y = 0, tile_passes = 0;
   long long T = 0, nb = 0, nd = 0, nt = 0;
-  size_t header = 0, depth_hist = 0, tile_hist = 0, status_bin = 0, status_dup = 0,
+  size_t header = 0, depth_hist = 0, tile_hist = 0, status_dup = 0,
          status_depth = 0, status_tile = 0, zero_bytes = 0;
   size_t rects = 0, records = 0, depth_keys[2] = {0, 0}, depth_vals[2] = {0, 0},
          tile_keys[2] = {0, 0}, tile_vals_tmp = 0;

@@ -46,17 +46,15 @@ struct PreprocessParams {
 constexpr size_t kPreprocessSmem = 8 * 32 * kShRestFloats * sizeof(float);
 
 __global__ void __launch_bounds__(kBinThreads) render_preprocess_kernel(PreprocessParams pp) {
-  __shared__ unsigned s_tile, s_prefix;
   __shared__ unsigned s_scan[33];
   __shared__ unsigned s_hist[4][256];
   __shared__ bool s_last;
   extern __shared__ __align__(16) float s_stage[];  // [8 warps][32 * 45]
   const BinParams& p = pp.bin;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
   for (int k = tid; k < 4 * 256; k += kBinThreads) (&s_hist[0][0])[k] = 0u;
   __syncthreads();
-  const int tile = (int)s_tile;
+  const int tile = (int)blockIdx.x;
   const int i = tile * kBinThreads + tid;
 
   Camera cam;
@@ -82,9 +80,7 @@ __global__ void __launch_bounds__(kBinThreads) render_preprocess_kernel(Preproce
     float* stage = s_stage + warp * 32 * kShRestFloats;
     warp_load_rows<kShRestFloats>(pp.k_j, tile * kBinThreads + warp * 32, p.N, stage);
     if (count > 0) {
-      float kj[kShRestFloats];
-#pragma unroll
-      for (int k = 0; k < kShRestFloats; ++k) kj[k] = stage[lane * kShRestFloats + k];
+      const float* kj = stage + lane * kShRestFloats;
       const float3 cp = make_float3(__ldg(pp.cam_pos), __ldg(pp.cam_pos + 1), __ldg(pp.cam_pos + 2));
       const float3 A = make_float3(__ldg(pp.albedo + 3 * i), __ldg(pp.albedo + 3 * i + 1),
                                    __ldg(pp.albedo + 3 * i + 2));
@@ -97,7 +93,7 @@ __global__ void __launch_bounds__(kBinThreads) render_preprocess_kernel(Preproce
                            __ldg(pp.opacity + i), depth_bits);
     }
   }
-  bin_block(p, tile, i, count, depth_bits, s_scan, s_hist, s_prefix, s_last);
+  bin_block(p, tile, i, count, depth_bits, s_scan, s_hist, s_last);
 }
 
 struct GaussianBwdParams {
@@ -127,7 +123,7 @@ __device__ __forceinline__ void put(float* p, float v, bool acc) {
   if (acc) *p += v; else *p = v;
 }
 
-__global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianBwdParams p) {
+__global__ void __launch_bounds__(256, 3) render_gaussian_backward_kernel(GaussianBwdParams p) {
   extern __shared__ __align__(16) float s_stage[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row0 = blockIdx.x * blockDim.x + warp * 32;
@@ -146,13 +142,8 @@ __global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianB
   float* stage = s_stage + warp * 32 * kShRestFloats;
   const bool warp_touched = __ballot_sync(0xffffffffu, touched) != 0u;
   if (warp_touched) warp_load_rows<kShRestFloats>(p.k_j, row0, p.N, stage);
-  float gkj[kShRestFloats];
-#pragma unroll
-  for (int k = 0; k < kShRestFloats; ++k) gkj[k] = 0.f;
+  float* row = stage + lane * kShRestFloats;
   if (valid && touched) {
-    float kj[kShRestFloats];
-#pragma unroll
-    for (int k = 0; k < kShRestFloats; ++k) kj[k] = stage[lane * kShRestFloats + k];
     // dL/dconic -> dL/dSigma2 = -V G V with G's off-diagonal half of the packed sum
     const float4 r1 = p.records[3 * i + 1];
     const float vx = r1.x, vy = r1.y, vz = r1.z;
@@ -174,7 +165,7 @@ __global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianB
     const float3 A = make_float3(__ldg(p.albedo + 3 * i), __ldg(p.albedo + 3 * i + 1),
                                  __ldg(p.albedo + 3 * i + 2));
     float3 gA;
-    const float3 gmu_sh = sh_backward(gcol, m, cp, A, kj, gA, gkj);
+    const float3 gmu_sh = sh_backward_inplace(gcol, m, cp, A, row, gA);
     put(p.g_mu + 3 * i, pg.mu.x + gmu_sh.x, acc);
     put(p.g_mu + 3 * i + 1, pg.mu.y + gmu_sh.y, acc);
     put(p.g_mu + 3 * i + 2, pg.mu.z + gmu_sh.z, acc);
@@ -210,11 +201,11 @@ __global__ void __launch_bounds__(256) render_gaussian_backward_kernel(GaussianB
     for (int k = 0; k < 3; ++k) p.g_albedo[3 * i + k] = 0.f;
     if (p.g_mean2d) p.g_mean2d[2 * i] = p.g_mean2d[2 * i + 1] = 0.f;
   }
-  // SH-rest gradient rows: staged, then written (or added) coalesced
+  // SH-rest gradient rows (computed in place in the stage; zero for untouched lanes), written
+  // or added coalesced
   if (warp_touched || !acc) {
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < kShRestFloats; ++k) stage[lane * kShRestFloats + k] = gkj[k];
+    if (!(valid && touched))
+      for (int k = 0; k < kShRestFloats; ++k) row[k] = 0.f;
     __syncwarp();
     if (acc) warp_add_rows<kShRestFloats>(p.g_k_j, row0, p.N, stage);
     else warp_store_rows<kShRestFloats>(p.g_k_j, row0, p.N, stage);
@@ -279,6 +270,8 @@ extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const flo
     GS_CUDA(cudaFuncSetAttribute(render_preprocess_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPreprocessSmem));
+    GS_CUDA(cudaFuncSetAttribute(render_preprocess_kernel,
+                                 cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     render_preprocess_kernel<<<(unsigned)L.nb, kBinThreads, kPreprocessSmem, st>>>(pp);
     GS_CHECK_LAUNCH();
   }
@@ -378,6 +371,8 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
   GS_CUDA(cudaFuncSetAttribute(render_gaussian_backward_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)kPreprocessSmem));
+  GS_CUDA(cudaFuncSetAttribute(render_gaussian_backward_kernel,
+                               cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   render_gaussian_backward_kernel<<<(N + 255) / 256, 256, kPreprocessSmem, st>>>(gp);
   GS_CHECK_LAUNCH();
   mark_stage(9, st);
