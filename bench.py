@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -317,7 +318,12 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--view-only", action="store_true",
+                    help="forward+backward of one config-2 view per step (single GPU); a small "
+                         "fixed workload for profiler captures of single kernels")
     args = ap.parse_args()
+    if args.view_only:
+        return run_view(args)
     args.warmup_ref = min(args.warmup, 1)
     rank, world, local = init_dist(args.gpus)
     try:
@@ -331,10 +337,44 @@ def main() -> int:
             dist.destroy_process_group()
 
 
+def run_view(args) -> int:
+    """One config-2 view (1M Gaussians, 1920x1080) rendered forward and backward through the
+    fused path per step, with a seeded upstream image gradient; prints per-stage ms."""
+    from custom_rasterizer_cuda import _lib
+    from custom_rasterizer_cuda.render import render_backward, render_forward
+    from gs3d_b200 import scenes
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    sc = scenes.config2(0, n=args.gaussians)
+    v = sc.views[0].as_dict(dev)
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    op = torch.sigmoid(al).reshape(-1).contiguous()
+    cam = (-torch.matmul(v["R"].T, v["T"])).reshape(3).contiguous()
+    g = torch.Generator("cpu").manual_seed(5)
+    grad_img = torch.rand(v["height"], v["width"], 3, generator=g).to(dev)
+    timer = StageTimer(args.steps)
+    for k in range(args.warmup + args.steps):
+        if k >= args.warmup:
+            timer.install_next()
+        img, _, st = render_forward(mu, q, s, op, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
+                                    v["cx"], v["cy"], v["height"], v["width"])
+        render_backward(st, grad_img, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
+                        v["cx"], v["cy"], want_mean2d_grad=False)
+    torch.cuda.synchronize()
+    timer.remove()
+    if _lib.device_error_bits() != 0:
+        raise RuntimeError(f"device error bits {_lib.device_error_bits():#x}")
+    print(json.dumps({"mode": "view", "workload": "config2 view 0: 1M Gaussians, 1920x1080",
+                      "steps": args.steps, "warmup": args.warmup, "pairs": st.pairs,
+                      "stage_ms": timer.stage_ms()}), flush=True)
+    return 0
+
+
 def run_ours(args, rank, world, local) -> int:
     import custom_rasterizer_cuda as crc
     from gs3d_b200 import scenes
-    from gs3d_b200.train_step import Trainer
+    from gs3d_b200.train_step import HostTargets, Trainer
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -369,22 +409,34 @@ def run_ours(args, rank, world, local) -> int:
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1), world)
     total_launches = int(sum_over_ranks(float(launches), world))
 
-    # ---- e2e: targets copied from pinned host memory each step, loss read back ----
+    # ---- e2e: every step copies its targets from pinned host memory (side stream, each view's
+    # loss waits for its own copy) and reads its loss back to the host (one step behind, so the
+    # host keeps the device fed); all of it inside the timed region ----
+    staged = HostTargets(host_targets, dev)
+    assert staged.bytes_per_step == h2d_bytes
+    trainer.step(staged)  # untimed: first use of the copy stream
+    loss_host = torch.empty(args.steps, dtype=torch.float32, pin_memory=True)
+    read = [torch.cuda.Event() for _ in range(args.steps)]
+    losses = []
     barrier(world)
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
-    dev_targets = list(trainer.targets)
-    for _ in range(args.steps):
-        for vi in mine:
-            dev_targets[vi] = host_targets[vi].to(dev, non_blocking=True)
-        loss = trainer.step(dev_targets)
-        float(loss.item())
+    for k in range(args.steps):
+        loss = trainer.step(staged)
+        loss_host[k].copy_(loss, non_blocking=True)
+        read[k].record()
+        if k > 0:
+            read[k - 1].synchronize()
+            losses.append(float(loss_host[k - 1]))
+    read[-1].synchronize()
+    losses.append(float(loss_host[-1]))
     t1.record()
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(t0.elapsed_time(t1), world)
+    assert len(losses) == args.steps and all(math.isfinite(x) for x in losses)
 
     value = BATCH_VIEWS * args.steps / (elapsed_ms * 1e-3)
     e2e_value = BATCH_VIEWS * args.steps / (e2e_ms * 1e-3)

@@ -270,4 +270,47 @@ static __global__ void __launch_bounds__(256) tile_ranges_kernel(const unsigned*
   }
 }
 
+// Launch order of the blend CTAs: tiles by decreasing list length, so the long serial
+// walks of crowded tiles start first and the short ones fill in behind them (with raster
+// order a crowded tile that starts late sets the kernel's end). Lengths are bucketed by
+// their leading bit and the two bits below it (129 buckets, descending); order within a
+// bucket is arbitrary. The outputs do not depend on the order. One CTA.
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderBuckets = 129;
+
+__device__ __forceinline__ int tile_order_bucket(int K) {
+  if (K <= 0) return 0;
+  const int lead = 31 - __clz(K);
+  const int next2 = lead >= 2 ? (K >> (lead - 2)) & 3 : (K << (2 - lead)) & 3;
+  return 1 + 4 * lead + next2;
+}
+
+static __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
+    const int2* __restrict__ ranges, const int* pair_count, long long pair_capacity,
+    int num_tiles, int* __restrict__ order) {
+  __shared__ unsigned s_hist[kOrderBuckets];
+  if ((long long)(*pair_count) > pair_capacity) return;  // the blend kernels return too
+  const int tid = threadIdx.x;
+  for (int b = tid; b < kOrderBuckets; b += kOrderThreads) s_hist[b] = 0u;
+  __syncthreads();
+  for (int t = tid; t < num_tiles; t += kOrderThreads) {
+    const int2 r = ranges[t];
+    atomicAdd(&s_hist[tile_order_bucket(r.y - r.x)], 1u);
+  }
+  __syncthreads();
+  if (tid == 0) {  // exclusive scan from the heaviest bucket down
+    unsigned run = 0;
+    for (int b = kOrderBuckets - 1; b >= 0; --b) {
+      const unsigned h = s_hist[b];
+      s_hist[b] = run;
+      run += h;
+    }
+  }
+  __syncthreads();
+  for (int t = tid; t < num_tiles; t += kOrderThreads) {
+    const int2 r = ranges[t];
+    order[atomicAdd(&s_hist[tile_order_bucket(r.y - r.x)], 1u)] = t;
+  }
+}
+
 }  // namespace gs

@@ -54,6 +54,7 @@ __device__ __forceinline__ bool warp_block_hit(float4 r0, float wx0, float wy0) 
 struct BlendFwdParams {
   int W, H, tiles_x;
   const int2* ranges;
+  const int* tile_order;  // CTA -> tile (tile_order_kernel); null: raster order
   const int* sorted_ids;
   const float4* records;
   const int* pair_count;
@@ -75,10 +76,11 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
   constexpr int kThreads = kTilePixels / kPix;
   __shared__ float4 s_rec[2][3][kBlendBatch];
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
-  const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
+  const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
+  const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
   const int tid = threadIdx.x;
   const BlendGeometry<kPix> geo(tile_x, tile_y);
-  const int2 range = p.ranges[blockIdx.x];
+  const int2 range = p.ranges[tile];
   const int K = range.y - range.x;
   const int nbatches = (K + kBlendBatch - 1) / kBlendBatch;
 
@@ -168,6 +170,7 @@ struct BlendBwdParams {
   int N, W, H, tiles_x;
   const float* grad_img;
   const int2* ranges;
+  const int* tile_order;  // CTA -> tile (tile_order_kernel); null: raster order
   const int* sorted_ids;
   const float4* records;  // 3 per Gaussian, indexed by Gaussian id
   const float* final_T;
@@ -249,10 +252,11 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
   __shared__ float4 s_rec[2][3][kBlendBatch];
   __shared__ float s_acc[kBlendBatch * kAccStride];
   __shared__ int s_max_last;
-  const int tile_x = blockIdx.x % p.tiles_x, tile_y = blockIdx.x / p.tiles_x;
+  const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
+  const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
   const int tid = threadIdx.x;
   const BlendGeometry<kPix> geo(tile_x, tile_y);
-  const int2 range = p.ranges[blockIdx.x];
+  const int2 range = p.ranges[tile];
   const int K = range.y - range.x;
 
   float gr[kPix], gg[kPix], gb[kPix], T[kPix], ar[kPix], ag[kPix], ab[kPix], fpy[kPix];

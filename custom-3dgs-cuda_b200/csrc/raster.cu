@@ -68,6 +68,7 @@ RasterLayout make_raster_layout(int N, int W, int H, long long capacity) {
   L.tile_keys[0] = take((size_t)capacity * sizeof(unsigned));
   L.tile_keys[1] = take((size_t)capacity * sizeof(unsigned));
   L.tile_vals_tmp = take((size_t)capacity * sizeof(unsigned));
+  L.tile_order = take((size_t)L.T * sizeof(int));
   L.total = off;
   L.nb = nb;
   L.nd = nd;
@@ -190,12 +191,18 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
       GS_CHECK_LAUNCH();
     }
   }
+  int* tile_order = reinterpret_cast<int*>(ws + L.tile_order);
+  tile_order_kernel<<<1, kOrderThreads, 0, stream>>>(reinterpret_cast<const int2*>(tile_ranges),
+                                                      &hdr->pair_count, capacity, (int)L.T,
+                                                      tile_order);
+  GS_CHECK_LAUNCH();
   mark_stage(5, stream);
   BlendFwdParams fp;
   fp.W = W;
   fp.H = H;
   fp.tiles_x = L.tiles_x;
   fp.ranges = reinterpret_cast<const int2*>(tile_ranges);
+  fp.tile_order = tile_order;
   fp.sorted_ids = sorted_ids;
   fp.records = records;
   fp.pair_count = &hdr->pair_count;
@@ -307,6 +314,7 @@ extern "C" int gs_rasterize_backward(int N, int H, int W, const float* grad_img,
   bp.tiles_x = tiles_x;
   bp.grad_img = grad_img;
   bp.ranges = reinterpret_cast<const int2*>(tile_ranges);
+  bp.tile_order = nullptr;  // raster order: this entry point has no forward workspace
   bp.sorted_ids = sorted_ids;
   bp.records = records;
   bp.final_T = final_T;

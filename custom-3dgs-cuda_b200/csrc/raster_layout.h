@@ -22,7 +22,7 @@ struct RasterLayout {
   size_t header = 0, depth_hist = 0, tile_hist = 0, status_dup = 0,
          status_depth = 0, status_tile = 0, zero_bytes = 0;
   size_t rects = 0, records = 0, depth_keys[2] = {0, 0}, depth_vals[2] = {0, 0},
-         tile_keys[2] = {0, 0}, tile_vals_tmp = 0;
+         tile_keys[2] = {0, 0}, tile_vals_tmp = 0, tile_order = 0;
   size_t total = 0;
 };
 

@@ -326,6 +326,8 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
   bp.tiles_x = L.tiles_x;
   bp.grad_img = grad_img;
   bp.ranges = reinterpret_cast<const int2*>(tile_ranges);
+  bp.tile_order =
+      reinterpret_cast<const int*>(static_cast<const char*>(fwd_workspace) + L.tile_order);
   bp.sorted_ids = sorted_ids;
   bp.records = records;
   bp.final_T = final_T;

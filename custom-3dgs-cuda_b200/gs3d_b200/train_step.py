@@ -123,6 +123,44 @@ def reduce_step(fg: FlatGrads, batch: int, world: int, group=None) -> None:
     fg.buffer[:fg.n_param].div_(float(batch))
 
 
+class HostTargets:
+    """Target images kept in pinned host memory and staged to the device every step.
+
+    `issue()` enqueues this step's host->device copies on a side stream, one per view, into
+    per-view device buffers; `get(vi)` makes the compute stream wait for view vi's copy only,
+    so the copies overlap the rendering of earlier views; `release(vi)` marks the buffer as
+    consumed by this step's loss, and the next step's copy into it waits for that mark.
+    """
+
+    def __init__(self, host: dict, device: torch.device):
+        self.host = host
+        self.dev = {vi: torch.empty(h.shape, dtype=h.dtype, device=device) for vi, h in host.items()}
+        self.stream = torch.cuda.Stream(device)
+        self.copied = {vi: torch.cuda.Event() for vi in host}
+        self.consumed = {vi: None for vi in host}
+
+    @property
+    def bytes_per_step(self) -> int:
+        return sum(h.numel() * h.element_size() for h in self.host.values())
+
+    def issue(self) -> None:
+        with torch.cuda.stream(self.stream):
+            for vi, h in self.host.items():
+                if self.consumed[vi] is not None:
+                    self.stream.wait_event(self.consumed[vi])
+                self.dev[vi].copy_(h, non_blocking=True)
+                self.copied[vi].record(self.stream)
+
+    def get(self, vi: int) -> torch.Tensor:
+        torch.cuda.current_stream(self.stream.device).wait_event(self.copied[vi])
+        return self.dev[vi]
+
+    def release(self, vi: int) -> None:
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.stream.device))
+        self.consumed[vi] = ev
+
+
 class Trainer:
     """Parameters, optimizer and flat gradient bucket of one rank.
 
@@ -173,6 +211,9 @@ class Trainer:
         from gs3d_b200.loss import l1_ssim_value_and_grad
 
         targets = self.targets if targets is None else targets
+        staged = isinstance(targets, HostTargets)
+        if staged:
+            targets.issue()
         g = self.gaussians
         fg = self.fg
         fg.zero()
@@ -191,7 +232,10 @@ class Trainer:
                 img, _, st = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
                                             v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
                                             v["width"])
-                loss, gimg = l1_ssim_value_and_grad(img, targets[vi], LAMBDA_DSSIM)
+                target = targets.get(vi) if staged else targets[vi]
+                loss, gimg = l1_ssim_value_and_grad(img, target, LAMBDA_DSSIM)
+                if staged:
+                    targets.release(vi)
                 render_backward(st, gimg, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
                                 v["cx"], v["cy"], want_mean2d_grad=False, out=out,
                                 stats=(fg.grad_norm_sum, fg.grad_count, fg.max_grad,
@@ -210,6 +254,9 @@ class Trainer:
         from gaussian_splatting.rasterizer.rasterize import RasterizeFunction, rasterize
 
         targets = self.targets if targets is None else targets
+        staged = isinstance(targets, HostTargets)
+        if staged:
+            targets.issue()
         self.fg.zero()
         self.fg.rebind(self.params)
         total = torch.zeros((), device=self.device)
@@ -218,13 +265,16 @@ class Trainer:
             if before_view is not None:
                 before_view(vi)
             img = rasterize(self.gaussians, view)
+            target = targets.get(vi) if staged else targets[vi]
             if self.fused_loss:
                 from gs3d_b200.loss import l1_ssim_loss
 
-                loss = l1_ssim_loss(img, targets[vi], LAMBDA_DSSIM)
+                loss = l1_ssim_loss(img, target, LAMBDA_DSSIM)
             else:
-                loss = reconstruction_loss(img, targets[vi], self.window)
+                loss = reconstruction_loss(img, target, self.window)
             loss.backward()
+            if staged:
+                targets.release(vi)
             accumulate_view_stats(self.fg, RasterizeFunction.last_mean2d_grad, view["width"],
                                   view["height"])
             total = total + loss.detach()
