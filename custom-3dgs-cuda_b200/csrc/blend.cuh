@@ -78,7 +78,7 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const BlendGeometry<kPix> geo(tile_x, tile_y);
   const int2 range = p.ranges[tile];
   const int K = range.y - range.x;
@@ -128,22 +128,30 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
     bool all_done = true;
 #pragma unroll
     for (int q = 0; q < kPix; ++q) all_done = all_done && done[q];
-    for (int i = 0; i < n && !all_done; ++i) {
-      const float4 r0 = rec[0][i];
-      if (!warp_block_hit<kPix>(r0, geo.wx0, geo.wy0)) continue;
-      const float4 r1 = rec[1][i];
-      const float dx = fpx - r0.x;
+    // 32 records at a time: each lane tests one against the warp's pixel block, the warp
+    // walks the hits in list order (pixels that are done skip them)
+    for (int k = 0; k < n && !__all_sync(0xffffffffu, all_done); k += 32) {
+      const int i_lane = k + lane;
+      const bool hit = i_lane < n && warp_block_hit<kPix>(rec[0][i_lane], geo.wx0, geo.wy0);
+      unsigned hits = __ballot_sync(0xffffffffu, hit);
+      while (hits) {
+        const int i = k + __ffs(hits) - 1;
+        hits &= hits - 1;
+        const float4 r0 = rec[0][i];
+        const float4 r1 = rec[1][i];
+        const float dx = fpx - r0.x;
 #pragma unroll
-      for (int q = 0; q < kPix; ++q) {
-        if (done[q]) continue;
-        const float dy = fpy[q] - r0.y;
-        const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
-        if (power > 0.0f) continue;
-        const float alpha = fminf(0.99f, __fmul_rn(r1.w, __expf(power)));
-        if (alpha < (1.0f / 255.0f)) continue;
-        blend_step(alpha, rec[2][i], T[q], cr[q], cg[q], cb[q]);
-        last[q] = b * kBlendBatch + i + 1;
-        if (T[q] < 1e-4f) done[q] = true;
+        for (int q = 0; q < kPix; ++q) {
+          if (done[q]) continue;
+          const float dy = fpy[q] - r0.y;
+          const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
+          if (power > 0.0f) continue;
+          const float alpha = fminf(0.99f, __fmul_rn(r1.w, __expf(power)));
+          if (alpha < (1.0f / 255.0f)) continue;
+          blend_step(alpha, rec[2][i], T[q], cr[q], cg[q], cb[q]);
+          last[q] = b * kBlendBatch + i + 1;
+          if (T[q] < 1e-4f) done[q] = true;
+        }
       }
       all_done = true;
 #pragma unroll
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
   __shared__ int s_max_last;
   const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const BlendGeometry<kPix> geo(tile_x, tile_y);
   const int2 range = p.ranges[tile];
   const int K = range.y - range.x;
@@ -329,58 +337,67 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
     __syncthreads();
     const int lo = batch_lo(b), hi = batch_hi(b);
     const float4(*rec)[kBlendBatch] = s_rec[b & 1];
-    for (int j = min(hi, warp_last) - 1; j >= lo; --j) {
-      const int k = j - lo;  // slot in this batch
-      const float4 r0 = rec[0][k];
-      if (!warp_block_hit<kPix>(r0, geo.wx0, geo.wy0)) continue;
-      float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      bool active = false;
-      const float4 r1 = rec[1][k];
-      const float cx = r1.x, cy = r1.y, cz = r1.z;
-      const float dx = fpx - r0.x;
+    // 32 list positions at a time from the back: lane l tests position top - 1 - l against
+    // the warp's pixel block, the warp walks the hits back to front
+    for (int top = min(hi, warp_last); top > lo; top -= 32) {
+      const int j_lane = top - 1 - lane;
+      const bool hit =
+          j_lane >= lo && warp_block_hit<kPix>(rec[0][j_lane - lo], geo.wx0, geo.wy0);
+      unsigned hits = __ballot_sync(0xffffffffu, hit);
+      while (hits) {
+        const int j = top - __ffs(hits);
+        hits &= hits - 1;
+        const int k = j - lo;  // slot in this batch
+        const float4 r0 = rec[0][k];
+        float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        bool active = false;
+        const float4 r1 = rec[1][k];
+        const float cx = r1.x, cy = r1.y, cz = r1.z;
+        const float dx = fpx - r0.x;
 #pragma unroll
-      for (int q = 0; q < kPix; ++q) {
-        if (j >= last[q]) continue;  // contributor j + 1 > n_contrib of this pixel
-        const float dy = fpy[q] - r0.y;
-        const float power = splat_power(make_float3(cx, cy, cz), dx, dy);
-        if (power > 0.0f) continue;
-        const float G = __expf(power);
-        const float alpha_raw = r1.w * G;
-        const float alpha = fminf(0.99f, alpha_raw);
-        if (alpha < (1.0f / 255.0f)) continue;
-        active = true;
-        const float4 r2 = rec[2][k];
-        const float one_minus = 1.0f - alpha;
-        // approximate division (2 ulp): the recovered T drifts by a few 1e-6 over a
-        // pixel's replay, far inside the gradient tolerance
-        const float T_before = __fdividef(T[q], fmaxf(one_minus, 1e-4f));
-        const float c0 = r2.x, c1 = r2.y, c2 = r2.z;
-        const float wgt = alpha * T_before;
-        v[5] += wgt * gr[q];
-        v[6] += wgt * gg[q];
-        v[7] += wgt * gb[q];
-        const float dL_dalpha =
-            ((c0 - ar[q]) * gr[q] + (c1 - ag[q]) * gg[q] + (c2 - ab[q]) * gb[q]) * T_before;
-        float dL_dpower = 0.0f;
-        if (alpha_raw < 0.99f) {
-          v[8] += G * dL_dalpha;
-          dL_dpower = alpha * dL_dalpha;
+        for (int q = 0; q < kPix; ++q) {
+          if (j >= last[q]) continue;  // contributor j + 1 > n_contrib of this pixel
+          const float dy = fpy[q] - r0.y;
+          const float power = splat_power(make_float3(cx, cy, cz), dx, dy);
+          if (power > 0.0f) continue;
+          const float G = __expf(power);
+          const float alpha_raw = r1.w * G;
+          const float alpha = fminf(0.99f, alpha_raw);
+          if (alpha < (1.0f / 255.0f)) continue;
+          active = true;
+          const float4 r2 = rec[2][k];
+          const float one_minus = 1.0f - alpha;
+          // approximate division (2 ulp): the recovered T drifts by a few 1e-6 over a
+          // pixel's replay, far inside the gradient tolerance
+          const float T_before = __fdividef(T[q], fmaxf(one_minus, 1e-4f));
+          const float c0 = r2.x, c1 = r2.y, c2 = r2.z;
+          const float wgt = alpha * T_before;
+          v[5] += wgt * gr[q];
+          v[6] += wgt * gg[q];
+          v[7] += wgt * gb[q];
+          const float dL_dalpha =
+              ((c0 - ar[q]) * gr[q] + (c1 - ag[q]) * gg[q] + (c2 - ab[q]) * gb[q]) * T_before;
+          float dL_dpower = 0.0f;
+          if (alpha_raw < 0.99f) {
+            v[8] += G * dL_dalpha;
+            dL_dpower = alpha * dL_dalpha;
+          }
+          v[0] += dL_dpower * (cx * dx + cy * dy);
+          v[1] += dL_dpower * (cy * dx + cz * dy);
+          v[2] += -0.5f * dL_dpower * dx * dx;
+          v[3] += -dL_dpower * dx * dy;
+          v[4] += -0.5f * dL_dpower * dy * dy;
+          ar[q] = alpha * c0 + one_minus * ar[q];
+          ag[q] = alpha * c1 + one_minus * ag[q];
+          ab[q] = alpha * c2 + one_minus * ab[q];
+          T[q] = T_before;
         }
-        v[0] += dL_dpower * (cx * dx + cy * dy);
-        v[1] += dL_dpower * (cy * dx + cz * dy);
-        v[2] += -0.5f * dL_dpower * dx * dx;
-        v[3] += -dL_dpower * dx * dy;
-        v[4] += -0.5f * dL_dpower * dy * dy;
-        ar[q] = alpha * c0 + one_minus * ar[q];
-        ag[q] = alpha * c1 + one_minus * ag[q];
-        ab[q] = alpha * c2 + one_minus * ab[q];
-        T[q] = T_before;
-      }
-      if (__any_sync(0xffffffffu, active)) {
-        float sum;
-        int slot;
-        warp_reduce9(v, &sum, &slot);
-        if (slot >= 0 && sum != 0.0f) atomicAdd(&s_acc[k * kAccStride + slot], sum);
+        if (__any_sync(0xffffffffu, active)) {
+          float sum;
+          int slot;
+          warp_reduce9(v, &sum, &slot);
+          if (slot >= 0 && sum != 0.0f) atomicAdd(&s_acc[k * kAccStride + slot], sum);
+        }
       }
     }
     __syncthreads();
