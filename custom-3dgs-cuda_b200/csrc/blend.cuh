@@ -248,6 +248,13 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // thread's pixels are summed, reduced per warp (warp_reduce9) and added into a per-batch shared
 // slot; after each batch the slot sums are flushed to the global gradients.
 //
+// Two rewrites keep the per-pixel work small (both linear, so only the rounding differs from
+// the reference's per-pixel expressions): the mean and conic gradients are accumulated as the
+// moments St = sum(dL/dpower dx), Su = sum(dL/dpower dy), sum(dL/dpower dx dx), sum(dL/dpower dx dy),
+// sum(dL/dpower dy dy) and multiplied by the splat's conic at the flush; and the three
+// accumulated colours behind the splat enter dL/dalpha only through their dot product with
+// dL/dpixel, so one scalar D replaces them (D' = alpha (c . g) + (1 - alpha) D).
+//
 // kFusedAccum selects the flush: false converts each tile's dL/dconic to dL/dSigma2 and adds
 // into the four reference-layout gradient arrays (9 scalar atomics, as the reference does);
 // true adds the raw sums into g_accum with vector atomics, 3 float4 per Gaussian:
@@ -267,14 +274,15 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
   const int2 range = p.ranges[tile];
   const int K = range.y - range.x;
 
-  float gr[kPix], gg[kPix], gb[kPix], T[kPix], ar[kPix], ag[kPix], ab[kPix], fpy[kPix];
+  // D = sum over channels of (colour accumulated behind the current splat) x dL/dpixel
+  float gr[kPix], gg[kPix], gb[kPix], T[kPix], D[kPix], fpy[kPix];
   int last[kPix];
   int my_last = 0;
 #pragma unroll
   for (int q = 0; q < kPix; ++q) {
     const int py = geo.py0 + 4 * q;
     gr[q] = gg[q] = gb[q] = T[q] = 0.0f;
-    ar[q] = ag[q] = ab[q] = 0.0f;
+    D[q] = 0.0f;
     last[q] = 0;
     fpy[q] = (float)py;
     if (geo.px < p.W && py < p.H) {
@@ -352,13 +360,12 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
         float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         bool active = false;
         const float4 r1 = rec[1][k];
-        const float cx = r1.x, cy = r1.y, cz = r1.z;
         const float dx = fpx - r0.x;
 #pragma unroll
         for (int q = 0; q < kPix; ++q) {
           if (j >= last[q]) continue;  // contributor j + 1 > n_contrib of this pixel
           const float dy = fpy[q] - r0.y;
-          const float power = splat_power(make_float3(cx, cy, cz), dx, dy);
+          const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
           if (power > 0.0f) continue;
           const float G = __expf(power);
           const float alpha_raw = r1.w * G;
@@ -370,26 +377,24 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
           // approximate division (2 ulp): the recovered T drifts by a few 1e-6 over a
           // pixel's replay, far inside the gradient tolerance
           const float T_before = __fdividef(T[q], fmaxf(one_minus, 1e-4f));
-          const float c0 = r2.x, c1 = r2.y, c2 = r2.z;
           const float wgt = alpha * T_before;
           v[5] += wgt * gr[q];
           v[6] += wgt * gg[q];
           v[7] += wgt * gb[q];
-          const float dL_dalpha =
-              ((c0 - ar[q]) * gr[q] + (c1 - ag[q]) * gg[q] + (c2 - ab[q]) * gb[q]) * T_before;
+          const float cdotg = r2.x * gr[q] + r2.y * gg[q] + r2.z * gb[q];
+          const float dL_dalpha = (cdotg - D[q]) * T_before;
           float dL_dpower = 0.0f;
           if (alpha_raw < 0.99f) {
             v[8] += G * dL_dalpha;
             dL_dpower = alpha * dL_dalpha;
           }
-          v[0] += dL_dpower * (cx * dx + cy * dy);
-          v[1] += dL_dpower * (cy * dx + cz * dy);
-          v[2] += -0.5f * dL_dpower * dx * dx;
-          v[3] += -dL_dpower * dx * dy;
-          v[4] += -0.5f * dL_dpower * dy * dy;
-          ar[q] = alpha * c0 + one_minus * ar[q];
-          ag[q] = alpha * c1 + one_minus * ag[q];
-          ab[q] = alpha * c2 + one_minus * ab[q];
+          const float tx = dL_dpower * dx, ty = dL_dpower * dy;
+          v[0] += tx;
+          v[1] += ty;
+          v[2] += tx * dx;
+          v[3] += tx * dy;
+          v[4] += ty * dy;
+          D[q] = alpha * cdotg + one_minus * D[q];
           T[q] = T_before;
         }
         if (__any_sync(0xffffffffu, active)) {
@@ -401,24 +406,27 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
       }
     }
     __syncthreads();
-    // flush this batch's slot sums to the global gradients
+    // flush this batch's slot sums to the global gradients; the moments become
+    // dL/dmean = (cx St + cy Su, cy St + cz Su) and dL/dconic = (-St.dx / 2, -St.dy, -Su.dy / 2)
     for (int t = tid; t < hi - lo; t += kThreads) {
       float* acc = &s_acc[t * kAccStride];
       const int g = __float_as_int(rec[2][t].w);
       bool any = false;
 #pragma unroll
       for (int q = 0; q < 9; ++q) any |= acc[q] != 0.0f;
+      const float4 r1 = rec[1][t];
+      const float vx = r1.x, vy = r1.y, vz = r1.z;
+      const float gmx = vx * acc[0] + vy * acc[1], gmy = vy * acc[0] + vz * acc[1];
+      const float gcx = -0.5f * acc[2], gcy = -acc[3], gcz = -0.5f * acc[4];
       if (kFusedAccum && any && g >= 0 && g < p.N) {
         float4* dst = p.g_accum + 3 * (size_t)g;
-        atomicAdd(dst, make_float4(acc[0], acc[1], acc[2], acc[3]));
-        atomicAdd(dst + 1, make_float4(acc[4], acc[8], acc[5], acc[6]));
+        atomicAdd(dst, make_float4(gmx, gmy, gcx, gcy));
+        atomicAdd(dst + 1, make_float4(gcz, acc[8], acc[5], acc[6]));
         atomicAdd(&dst[2].x, acc[7]);
       } else if (any && g >= 0 && g < p.N) {
-        atomicAdd(p.g_mean2d + 2 * g, acc[0]);
-        atomicAdd(p.g_mean2d + 2 * g + 1, acc[1]);
-        const float4 r1 = rec[1][t];
-        const float vx = r1.x, vy = r1.y, vz = r1.z;
-        const float gx = acc[2], gy = 0.5f * acc[3], gz = acc[4];
+        atomicAdd(p.g_mean2d + 2 * g, gmx);
+        atomicAdd(p.g_mean2d + 2 * g + 1, gmy);
+        const float gx = gcx, gy = 0.5f * gcy, gz = gcz;
         atomicAdd(p.g_cov2d + 3 * g, -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz));
         atomicAdd(p.g_cov2d + 3 * g + 1,
                   -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz));
