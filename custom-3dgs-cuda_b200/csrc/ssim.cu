@@ -3,9 +3,11 @@
 // C1 = 0.01^2, C2 = 0.03^2), averaged over pixels and channels.
 //
 // Forward (one kernel + a one-block reduction): each CTA stages a 32x16 output tile plus a
-// 5-pixel halo of x and y in shared memory, blurs the five moments (x, y, x^2, y^2, xy) of the
-// three channels separably (11 horizontal taps into shared memory, then 11 vertical taps),
-// forms the SSIM map and, per pixel and channel, the three derivative maps
+// 5-pixel halo of x and y in shared memory (one plane per channel), blurs the five moments
+// (x, y, x^2, y^2, xy) of the three channels separably (11 horizontal taps into shared memory,
+// then 11 vertical taps; each thread produces a run of 8 outputs from an 18-value window held
+// in registers, so a tap costs an FMA and no shared-memory load), forms the SSIM map and, per
+// pixel and channel, the three derivative maps (stored planar, one plane per map and channel)
 //   B  = dS/dE[x^2] = -S / (var_x + var_y + C2)
 //   Cm = dS/dE[xy]  = 2 (2 mu_x mu_y + C1) / den
 //   A  = dS/dmu_x - 2 mu_x B - mu_y Cm
@@ -20,80 +22,157 @@ namespace gs {
 constexpr int kSsimTW = 32, kSsimTH = 16, kSsimR = 5, kSsimTaps = 11;
 constexpr int kSsimInW = kSsimTW + 2 * kSsimR;  // 42
 constexpr int kSsimInH = kSsimTH + 2 * kSsimR;  // 26
-constexpr int kSsimThreads = 256;
+constexpr int kSsimRun = 8;                     // outputs per thread and blur pass
+constexpr int kSsimWin = kSsimRun + kSsimTaps - 1;  // 18 inputs per run
+constexpr int kSsimThreads = 192;
+constexpr int kSsimWarps = kSsimThreads / 32;
 constexpr float kSsimC1 = 0.01f * 0.01f, kSsimC2 = 0.03f * 0.03f;
+static_assert(kSsimTW % kSsimRun == 0 && kSsimTH % kSsimRun == 0, "runs tile the output");
+static_assert(3 * kSsimTW * (kSsimTH / kSsimRun) == kSsimThreads, "one vertical run per thread");
 
 __constant__ float c_gauss[kSsimTaps];
 
+// Planar per-channel staging; h holds the horizontal blurs of the 5 moments of 3 channels.
 struct SsimForwardSmem {
-  float x[kSsimInH][kSsimInW][3];
-  float y[kSsimInH][kSsimInW][3];
-  float h[15][kSsimInH][kSsimTW];  // horizontal blurs: 5 moments x 3 channels
-  double part[2][kSsimThreads / 32];
+  float x[3][kSsimInH][kSsimInW];
+  float y[3][kSsimInH][kSsimInW];
+  float h[15][kSsimInH][kSsimTW];
+  double part[2][kSsimWarps];
 };
 
 struct SsimBackwardSmem {
-  float m[kSsimInH][kSsimInW][9];  // A, B, Cm x 3 channels
+  float m[9][kSsimInH][kSsimInW];  // A, B, Cm x 3 channels
   float h[9][kSsimInH][kSsimTW];
 };
 
-__device__ __forceinline__ float load_px(const float* img, int W, int H, int x, int y, int c) {
-  return (x >= 0 && x < W && y >= 0 && y < H) ? __ldg(img + ((size_t)y * W + x) * 3 + c) : 0.0f;
+// out[o] = sum_t g[t] in[o + t] for a run of kSsimRun outputs (registers only).
+__device__ __forceinline__ void blur_run(const float (&in)[kSsimWin], float (&out)[kSsimRun]) {
+#pragma unroll
+  for (int o = 0; o < kSsimRun; ++o) {
+    float v = 0.f;
+#pragma unroll
+    for (int t = 0; t < kSsimTaps; ++t) v += c_gauss[t] * in[o + t];
+    out[o] = v;
+  }
 }
 
+__device__ __forceinline__ void load_row_window(const float* row, float (&w)[kSsimWin]) {
+  const float2* r2 = reinterpret_cast<const float2*>(row);  // 8-byte aligned: even offsets
+#pragma unroll
+  for (int k = 0; k < kSsimWin / 2; ++k) {
+    const float2 v = r2[k];
+    w[2 * k] = v.x;
+    w[2 * k + 1] = v.y;
+  }
+}
+
+__device__ __forceinline__ void store_run(float* dst, const float (&v)[kSsimRun]) {
+  float4* d4 = reinterpret_cast<float4*>(dst);  // 16-byte aligned: offsets of 8 floats
+#pragma unroll
+  for (int k = 0; k < kSsimRun / 4; ++k)
+    d4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
+// Derivative maps are planar: maps[(3 * kind + channel) * H * W + pixel], kind A, B, Cm.
 __global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
     int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
     float* __restrict__ maps, double* __restrict__ partials) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SsimForwardSmem& s = *reinterpret_cast<SsimForwardSmem*>(smem_raw);
   const int tid = threadIdx.x;
-  const int x0 = blockIdx.x * kSsimTW - kSsimR, y0 = blockIdx.y * kSsimTH - kSsimR;
-  for (int i = tid; i < kSsimInH * kSsimInW * 3; i += kSsimThreads) {
-    const int c = i % 3, px = (i / 3) % kSsimInW, py = i / (3 * kSsimInW);
-    s.x[py][px][c] = load_px(img, W, H, x0 + px, y0 + py, c);
-    s.y[py][px][c] = load_px(ref, W, H, x0 + px, y0 + py, c);
-  }
-  __syncthreads();
-  for (int i = tid; i < kSsimInH * kSsimTW; i += kSsimThreads) {
-    const int r = i / kSsimTW, col = i % kSsimTW;
+  const int bx = blockIdx.x * kSsimTW, by = blockIdx.y * kSsimTH;
+  const int x0 = bx - kSsimR, y0 = by - kSsimR;
+  double l1_sum = 0.0;
+  // coalesced loads of the interleaved rows, de-interleaved into planes; the L1 term is
+  // summed here over the tile's own (non-halo) pixels
+  // one warp per halo row (126 interleaved floats, lanes along the row), all of a warp's rows
+  // loaded before any is stored
+  {
+    constexpr int kRowF = kSsimInW * 3;
+    constexpr int kRowsPerWarp = (kSsimInH + kSsimWarps - 1) / kSsimWarps;
+    constexpr int kChunks = (kRowF + 31) / 32;
+    const int warp = tid >> 5, lane = tid & 31;
+    float a[kRowsPerWarp][kChunks], b[kRowsPerWarp][kChunks];
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      float mx = 0.f, my = 0.f, xx = 0.f, yy = 0.f, xy = 0.f;
+    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+      const int py = warp + rr * kSsimWarps, gy = y0 + py;
+      const bool row_ok = py < kSsimInH && gy >= 0 && gy < H;
 #pragma unroll
-      for (int k = 0; k < kSsimTaps; ++k) {
-        const float g = c_gauss[k], a = s.x[r][col + k][c], b = s.y[r][col + k][c];
-        mx += g * a;
-        my += g * b;
-        xx += g * (a * a);
-        yy += g * (b * b);
-        xy += g * (a * b);
+      for (int u = 0; u < kChunks; ++u) {
+        const int f = lane + 32 * u, gf = 3 * x0 + f;
+        a[rr][u] = b[rr][u] = 0.f;
+        if (row_ok && f < kRowF && gf >= 0 && gf < 3 * W) {
+          const size_t o = (size_t)gy * W * 3 + gf;
+          a[rr][u] = __ldg(img + o);
+          b[rr][u] = __ldg(ref + o);
+        }
       }
-      s.h[c * 5 + 0][r][col] = mx;
-      s.h[c * 5 + 1][r][col] = my;
-      s.h[c * 5 + 2][r][col] = xx;
-      s.h[c * 5 + 3][r][col] = yy;
-      s.h[c * 5 + 4][r][col] = xy;
+    }
+#pragma unroll
+    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+      const int py = warp + rr * kSsimWarps;
+      if (py >= kSsimInH) break;
+#pragma unroll
+      for (int u = 0; u < kChunks; ++u) {
+        const int f = lane + 32 * u;
+        if (f >= kRowF) break;
+        const int px = f / 3, c = f - 3 * px;
+        if (px >= kSsimR && px < kSsimR + kSsimTW && py >= kSsimR && py < kSsimR + kSsimTH)
+          l1_sum += (double)fabsf(a[rr][u] - b[rr][u]);  // zero outside the image
+        s.x[c][py][px] = a[rr][u];
+        s.y[c][py][px] = b[rr][u];
+      }
     }
   }
   __syncthreads();
-  double ssim_sum = 0.0, l1_sum = 0.0;
-  for (int i = tid; i < kSsimTH * kSsimTW; i += kSsimThreads) {
-    const int oy = i / kSsimTW, ox = i % kSsimTW;
-    const int gx = blockIdx.x * kSsimTW + ox, gy = blockIdx.y * kSsimTH + oy;
-    if (gx >= W || gy >= H) continue;
-    float out[9];
+  // horizontal: one run of 8 outputs of the 5 moments of one channel per item
+  for (int it = tid; it < 3 * kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
+    const int c = it / (kSsimInH * (kSsimTW / kSsimRun));
+    const int rem = it - c * (kSsimInH * (kSsimTW / kSsimRun));
+    const int r = rem / (kSsimTW / kSsimRun), cb = rem - r * (kSsimTW / kSsimRun);
+    float xa[kSsimWin], ya[kSsimWin], w[kSsimWin], out[kSsimRun];
+    load_row_window(&s.x[c][r][cb * kSsimRun], xa);
+    load_row_window(&s.y[c][r][cb * kSsimRun], ya);
+    blur_run(xa, out);
+    store_run(&s.h[c * 5 + 0][r][cb * kSsimRun], out);
+    blur_run(ya, out);
+    store_run(&s.h[c * 5 + 1][r][cb * kSsimRun], out);
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      float m[5];
+    for (int k = 0; k < kSsimWin; ++k) w[k] = xa[k] * xa[k];
+    blur_run(w, out);
+    store_run(&s.h[c * 5 + 2][r][cb * kSsimRun], out);
 #pragma unroll
-      for (int q = 0; q < 5; ++q) {
-        float v = 0.f;
+    for (int k = 0; k < kSsimWin; ++k) w[k] = ya[k] * ya[k];
+    blur_run(w, out);
+    store_run(&s.h[c * 5 + 3][r][cb * kSsimRun], out);
 #pragma unroll
-        for (int k = 0; k < kSsimTaps; ++k) v += c_gauss[k] * s.h[c * 5 + q][oy + k][ox];
-        m[q] = v;
-      }
-      const float mx = m[0], my = m[1];
-      const float vx = m[2] - mx * mx, vy = m[3] - my * my, cxy = m[4] - mx * my;
+    for (int k = 0; k < kSsimWin; ++k) w[k] = xa[k] * ya[k];
+    blur_run(w, out);
+    store_run(&s.h[c * 5 + 4][r][cb * kSsimRun], out);
+  }
+  __syncthreads();
+  // vertical: each thread one column run of 8 pixels of one channel
+  double ssim_sum = 0.0;
+  {
+    const int c = tid / (kSsimTW * (kSsimTH / kSsimRun));
+    const int rem = tid - c * (kSsimTW * (kSsimTH / kSsimRun));
+    const int rb = rem / kSsimTW, col = rem - rb * kSsimTW;
+    float m[5][kSsimRun];
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {
+      float v[kSsimWin];
+#pragma unroll
+      for (int k = 0; k < kSsimWin; ++k) v[k] = s.h[c * 5 + q][rb * kSsimRun + k][col];
+      blur_run(v, m[q]);
+    }
+    const int gx = bx + col;
+    const size_t HW = (size_t)H * W;
+#pragma unroll
+    for (int o = 0; o < kSsimRun; ++o) {
+      const int gy = by + rb * kSsimRun + o;
+      if (gx >= W || gy >= H) continue;
+      const float mx = m[0][o], my = m[1][o];
+      const float vx = m[2][o] - mx * mx, vy = m[3][o] - my * my, cxy = m[4][o] - mx * my;
       const float n1 = 2.f * mx * my + kSsimC1, n2 = 2.f * cxy + kSsimC2;
       const float d1 = mx * mx + my * my + kSsimC1, d2 = vx + vy + kSsimC2;
       const float den = d1 * d2;
@@ -102,16 +181,12 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
       const float Cm = 2.f * n1 / den;
       const float dmx = (2.f * my * n2) / den - S * (2.f * mx) / d1;
       const float A = dmx - 2.f * mx * B - my * Cm;
-      out[c] = A;
-      out[3 + c] = B;
-      out[6 + c] = Cm;
+      const size_t pix = (size_t)gy * W + gx;
+      maps[(0 + c) * HW + pix] = A;
+      maps[(3 + c) * HW + pix] = B;
+      maps[(6 + c) * HW + pix] = Cm;
       ssim_sum += (double)S;
-      const float xv = s.x[oy + kSsimR][ox + kSsimR][c], yv = s.y[oy + kSsimR][ox + kSsimR][c];
-      l1_sum += (double)fabsf(xv - yv);
     }
-    float* dst = maps + ((size_t)gy * W + gx) * 9;
-#pragma unroll
-    for (int q = 0; q < 9; ++q) dst[q] = out[q];
   }
   // block reduction in a fixed order
 #pragma unroll
@@ -126,7 +201,7 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
   __syncthreads();
   if (tid == 0) {
     double a = 0.0, b = 0.0;
-    for (int w = 0; w < kSsimThreads / 32; ++w) {
+    for (int w = 0; w < kSsimWarps; ++w) {
       a += s.part[0][w];
       b += s.part[1][w];
     }
@@ -170,47 +245,78 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_backward_kernel(
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SsimBackwardSmem& s = *reinterpret_cast<SsimBackwardSmem*>(smem_raw);
   const int tid = threadIdx.x;
-  const int x0 = blockIdx.x * kSsimTW - kSsimR, y0 = blockIdx.y * kSsimTH - kSsimR;
-  for (int i = tid; i < kSsimInH * kSsimInW * 9; i += kSsimThreads) {
-    const int q = i % 9, px = (i / 9) % kSsimInW, py = i / (9 * kSsimInW);
-    const int gx = x0 + px, gy = y0 + py;
-    s.m[py][px][q] =
-        (gx >= 0 && gx < W && gy >= 0 && gy < H) ? __ldg(maps + ((size_t)gy * W + gx) * 9 + q) : 0.f;
+  const int bx = blockIdx.x * kSsimTW, by = blockIdx.y * kSsimTH;
+  const int x0 = bx - kSsimR, y0 = by - kSsimR;
+  const size_t HW = (size_t)H * W;
+  {
+    // one warp per halo row of one map plane (lanes along the row), 8 rows in flight per warp
+    constexpr int kRows = 9 * kSsimInH;
+    constexpr int kRowsPerWarp = (kRows + kSsimWarps - 1) / kSsimWarps;
+    constexpr int kBatch = 8;
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll 1
+    for (int r0 = 0; r0 < kRowsPerWarp; r0 += kBatch) {
+      float v[kBatch][2];
+#pragma unroll
+      for (int rr = 0; rr < kBatch; ++rr) {
+        const int row = warp + (r0 + rr) * kSsimWarps;
+        const int q = row / kSsimInH, py = row - q * kSsimInH, gy = y0 + py;
+        const bool row_ok = r0 + rr < kRowsPerWarp && row < kRows && gy >= 0 && gy < H;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int px = lane + 32 * u, gx = x0 + px;
+          v[rr][u] = (row_ok && px < kSsimInW && gx >= 0 && gx < W)
+                         ? __ldg(maps + q * HW + (size_t)gy * W + gx)
+                         : 0.f;
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < kBatch; ++rr) {
+        const int row = warp + (r0 + rr) * kSsimWarps;
+        if (r0 + rr >= kRowsPerWarp || row >= kRows) break;
+        const int q = row / kSsimInH, py = row - q * kSsimInH;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int px = lane + 32 * u;
+          if (px < kSsimInW) s.m[q][py][px] = v[rr][u];
+        }
+      }
+    }
   }
   __syncthreads();
-  for (int i = tid; i < kSsimInH * kSsimTW; i += kSsimThreads) {
-    const int r = i / kSsimTW, col = i % kSsimTW;
-#pragma unroll
-    for (int q = 0; q < 9; ++q) {
-      float v = 0.f;
-#pragma unroll
-      for (int k = 0; k < kSsimTaps; ++k) v += c_gauss[k] * s.m[r][col + k][q];
-      s.h[q][r][col] = v;
-    }
+  for (int it = tid; it < 9 * kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
+    const int q = it / (kSsimInH * (kSsimTW / kSsimRun));
+    const int rem = it - q * (kSsimInH * (kSsimTW / kSsimRun));
+    const int r = rem / (kSsimTW / kSsimRun), cb = rem - r * (kSsimTW / kSsimRun);
+    float w[kSsimWin], out[kSsimRun];
+    load_row_window(&s.m[q][r][cb * kSsimRun], w);
+    blur_run(w, out);
+    store_run(&s.h[q][r][cb * kSsimRun], out);
   }
   __syncthreads();
   const float g = __ldg(grad_loss);
   const float w_l1 = g * (1.0f - lambda) * inv_n, w_ssim = -g * lambda * inv_n;
-  for (int i = tid; i < kSsimTH * kSsimTW; i += kSsimThreads) {
-    const int oy = i / kSsimTW, ox = i % kSsimTW;
-    const int gx = blockIdx.x * kSsimTW + ox, gy = blockIdx.y * kSsimTH + oy;
+  const int c = tid / (kSsimTW * (kSsimTH / kSsimRun));
+  const int rem = tid - c * (kSsimTW * (kSsimTH / kSsimRun));
+  const int rb = rem / kSsimTW, col = rem - rb * kSsimTW;
+  float bl[3][kSsimRun];
+#pragma unroll
+  for (int kind = 0; kind < 3; ++kind) {
+    float v[kSsimWin];
+#pragma unroll
+    for (int k = 0; k < kSsimWin; ++k) v[k] = s.h[3 * kind + c][rb * kSsimRun + k][col];
+    blur_run(v, bl[kind]);
+  }
+  const int gx = bx + col;
+#pragma unroll
+  for (int o = 0; o < kSsimRun; ++o) {
+    const int gy = by + rb * kSsimRun + o;
     if (gx >= W || gy >= H) continue;
-    const size_t p = ((size_t)gy * W + gx) * 3;
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      float bA = 0.f, bB = 0.f, bC = 0.f;
-#pragma unroll
-      for (int k = 0; k < kSsimTaps; ++k) {
-        const float gk = c_gauss[k];
-        bA += gk * s.h[c][oy + k][ox];
-        bB += gk * s.h[3 + c][oy + k][ox];
-        bC += gk * s.h[6 + c][oy + k][ox];
-      }
-      const float xv = __ldg(img + p + c), yv = __ldg(ref + p + c);
-      const float d = xv - yv;
-      const float sgn = d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
-      grad_img[p + c] = w_l1 * sgn + w_ssim * (bA + 2.f * xv * bB + yv * bC);
-    }
+    const size_t p = ((size_t)gy * W + gx) * 3 + c;
+    const float xv = __ldg(img + p), yv = __ldg(ref + p);
+    const float d = xv - yv;
+    const float sgn = d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
+    grad_img[p] = w_l1 * sgn + w_ssim * (bl[0][o] + 2.f * xv * bl[1][o] + yv * bl[2][o]);
   }
 }
 

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import c_float, c_int, c_longlong, c_size_t, c_uint, c_void_p, POINTER
+from ctypes import c_double, c_float, c_int, c_longlong, c_size_t, c_uint, c_void_p, POINTER
 from pathlib import Path
 
 # The library built in-tree by build.py; GS3D_B200_LIB may point at another build of it.
@@ -53,6 +53,7 @@ SIGNATURES = {
     "gs_l1_ssim_workspace_size": (c_size_t, [c_int, c_int]),
     "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
+    "gs_adam_step": (c_int, [c_int, P, P, P, P, P, P, c_double, c_double, c_double, c_longlong, P]),
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),

@@ -187,11 +187,16 @@ class Trainer:
         self.targets = targets
         self.plan = ShardPlan(rank, world, len(views))
         self.window = gaussian_window(device=device)
-        groups = [{"params": [getattr(g, n)], "lr": LEARNING_RATES[n], "name": n}
-                  for n in PARAM_NAMES]
-        kw = {"fused": True} if (fused_adam and device.type == "cuda") else {}
-        self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15, **kw)
         self.fg = FlatGrads(self.params, scene.N)
+        if fused_adam and device.type == "cuda":
+            from gs3d_b200.optim import FlatAdam
+
+            self.opt = FlatAdam(self.params, [LEARNING_RATES[n] for n in PARAM_NAMES],
+                                list(PARAM_NAMES), self.fg.buffer, eps=1e-15)
+        else:
+            groups = [{"params": [getattr(g, n)], "lr": LEARNING_RATES[n], "name": n}
+                      for n in PARAM_NAMES]
+            self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15)
         self.fused_loss = fused_loss and device.type == "cuda"
         if mode not in ("direct", "autograd"):
             raise ValueError(f"unknown trainer mode {mode!r}")

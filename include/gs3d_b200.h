@@ -197,6 +197,21 @@ GS_API int gs_l1_ssim_backward(int H, int W, const float* img, const float* targ
                                const float* grad_loss, float* grad_img, void* stream);
 
 /*
+ * One Adam step (torch.optim.Adam semantics, amsgrad off, no weight decay; the reference's
+ * trainer builds torch.optim.Adam(params, eps=1e-15), gaussian_splatting/utils/optim.py:31) over
+ * n_groups <= 8 parameter tensors in one launch. Group k has sizes[k] elements at params[k]
+ * and learning rate lrs[k] (host arrays); its gradients and moments are the slice starting at
+ * sizes[0] + ... + sizes[k-1] of the flat device buffers grad, exp_avg and exp_avg_sq. `step` is
+ * the 1-based step count used for bias correction; 1 - beta1, 1 - beta2 and the bias corrections
+ * are formed in double on the host, as torch forms them from Python floats. No counterpart in the reference's
+ * extension (its trainer calls torch's optimizer).
+ */
+GS_API int gs_adam_step(int n_groups, float* const* params, const long long* sizes,
+                        const float* lrs, const float* grad, float* exp_avg, float* exp_avg_sq,
+                        double beta1, double beta2, double eps, long long step,
+                        void* stream);
+
+/*
  * CUDA event helpers for m_ready_event (cudaEvent_t values passed as void*): create an event
  * with timing disabled, block the calling thread until it completes, destroy it.
  */
