@@ -215,6 +215,15 @@ def view_pair_stats(trainer, views: list[dict]) -> dict:
     return {"pairs": pairs, "replayed_pairs": replayed}
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each stage's kernel,
+# from one `ncu --set full --clock-control none` capture of a config-2 view (1M Gaussians of
+# the config-4 distribution at 1920x1080: `bench.py --view-only --steps 1 --warmup 1`).
+NCU_DRAM_BYTES = {
+    "preprocess": 259.9e6, "duplicate": 13.8e6, "blend_forward": 73.5e6,
+    "blend_backward": 142.7e6, "gaussian_backward": 490.0e6,
+}
+
+
 def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int) -> dict:
     """Roofline of the dominant stage over the timed region. The blends are FP32-issue bound
     (no dense contraction anywhere on the path); the per-Gaussian stages are HBM bound."""
@@ -234,13 +243,15 @@ def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n:
     if name in hbm_bytes:
         achieved = hbm_bytes[name] / (ms * 1e-3) / 1e9
         return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                "traffic": NCU_DRAM_BYTES.get(name),
                 "peak_source": pk["source"], "ms_per_launch": ms}
     fp32_peak = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6 / 1e12  # TFLOP/s
     flops_per_pair = 40.0 if name == "blend_backward" else 14.0
     achieved = flops_per_pair * mean_replayed / (ms * 1e-3) / 1e12
     return {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": fp32_peak,
-            "unit": "TFLOP/s", "frac": achieved / fp32_peak, "traffic": None,
+            "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+            "traffic": NCU_DRAM_BYTES.get(name), "traffic_unit": "bytes per launch (ncu)",
             "peak_source": "derived: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz",
             "ms_per_launch": ms,
             "unit_of_work": f"{flops_per_pair:.0f} FLOP per replayed (pixel, Gaussian) pair, "
