@@ -110,6 +110,8 @@ def init_dist(n_gpus: int):
     if world > 1:
         import datetime
 
+        # NCCL writes its banner and debug lines to stdout; keep stdout for the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))

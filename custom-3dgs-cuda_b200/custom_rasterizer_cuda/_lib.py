@@ -54,6 +54,8 @@ SIGNATURES = {
     "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_adam_step": (c_int, [c_int, P, P, P, P, P, P, c_double, c_double, c_double, c_longlong, P]),
+    "gs_sharded_adam_step": (c_int, [P, P, P, c_int, P, P, c_double, c_double, c_double,
+                                     c_longlong, c_float, P]),
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),

@@ -74,15 +74,23 @@ class ShardPlan:
 
 
 class FlatGrads:
-    """One contiguous fp32 buffer backing the .grad of every parameter, followed by the
-    densification sums (per Gaussian: norm sum, count)."""
+    """One contiguous fp32 buffer backing the .grad of every parameter, followed (at
+    `stats_offset`, default right after the gradients) by the densification sums (per Gaussian:
+    norm sum, count). `buffer` / `max_grad` may be given (the sharded step's symmetric
+    buffers); otherwise they are allocated here."""
 
-    def __init__(self, params: list[torch.Tensor], n_gaussians: int):
+    def __init__(self, params: list[torch.Tensor], n_gaussians: int, buffer=None,
+                 stats_offset: int | None = None, max_grad=None):
         sizes = [p.numel() for p in params]
         self.n_param = sum(sizes)
         self.n = n_gaussians
         dev = params[0].device
-        self.buffer = torch.zeros(self.n_param + 2 * n_gaussians, device=dev, dtype=torch.float32)
+        so = self.n_param if stats_offset is None else stats_offset
+        if buffer is None:
+            buffer = torch.zeros(so + 2 * n_gaussians, device=dev, dtype=torch.float32)
+        if buffer.numel() < so + 2 * n_gaussians or so < self.n_param:
+            raise ValueError("gradient bucket too small for the parameters and statistics")
+        self.buffer = buffer
         off = 0
         self.views = []
         for p, k in zip(params, sizes):
@@ -90,9 +98,10 @@ class FlatGrads:
             p.grad = v
             self.views.append(v)
             off += k
-        self.grad_norm_sum = self.buffer[self.n_param:self.n_param + n_gaussians]
-        self.grad_count = self.buffer[self.n_param + n_gaussians:]
-        self.max_grad = torch.zeros(n_gaussians, device=dev, dtype=torch.float32)
+        self.grad_norm_sum = self.buffer[so:so + n_gaussians]
+        self.grad_count = self.buffer[so + n_gaussians:so + 2 * n_gaussians]
+        self.max_grad = (torch.zeros(n_gaussians, device=dev, dtype=torch.float32)
+                         if max_grad is None else max_grad)
 
     def zero(self) -> None:
         self.buffer.zero_()
@@ -179,21 +188,38 @@ class Trainer:
         self.device = device
         self.rank, self.world, self.group = rank, world, group
         g = gaussian(scene.N)
-        for name, t in zip(PARAM_NAMES, scene.params()):
-            setattr(g, name, torch.nn.Parameter(t.to(device).contiguous()))
+        lrs = [LEARNING_RATES[n] for n in PARAM_NAMES]
+        # several CUDA ranks: parameters, gradients and statistics in symmetric memory, and one
+        # fused reduce-scatter + Adam + all-gather kernel per step (gs3d_b200.sharded)
+        self.sharded = None
+        if world > 1 and device.type == "cuda" and fused_adam:
+            from gs3d_b200.sharded import ShardedStep
+
+            self.sharded = ShardedStep(list(scene.params()), list(PARAM_NAMES), lrs, scene.N,
+                                       len(views), device, group, eps=1e-15)
+            for name, v in zip(PARAM_NAMES, self.sharded.param_views):
+                setattr(g, name, torch.nn.Parameter(v))
+        else:
+            for name, t in zip(PARAM_NAMES, scene.params()):
+                setattr(g, name, torch.nn.Parameter(t.to(device).contiguous()))
         self.gaussians = g
         self.params = [getattr(g, n) for n in PARAM_NAMES]
         self.views = [v.as_dict(device) for v in views]
         self.targets = targets
         self.plan = ShardPlan(rank, world, len(views))
         self.window = gaussian_window(device=device)
-        self.fg = FlatGrads(self.params, scene.N)
-        if fused_adam and device.type == "cuda":
+        if self.sharded is not None:
+            self.fg = FlatGrads(self.params, scene.N, buffer=self.sharded.bucket,
+                                stats_offset=self.sharded.layout.stats_offset,
+                                max_grad=self.sharded.max_stat)
+            self.opt = self.sharded
+        elif fused_adam and device.type == "cuda":
             from gs3d_b200.optim import FlatAdam
 
-            self.opt = FlatAdam(self.params, [LEARNING_RATES[n] for n in PARAM_NAMES],
-                                list(PARAM_NAMES), self.fg.buffer, eps=1e-15)
+            self.fg = FlatGrads(self.params, scene.N)
+            self.opt = FlatAdam(self.params, lrs, list(PARAM_NAMES), self.fg.buffer, eps=1e-15)
         else:
+            self.fg = FlatGrads(self.params, scene.N)
             groups = [{"params": [getattr(g, n)], "lr": LEARNING_RATES[n], "name": n}
                       for n in PARAM_NAMES]
             self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15)
@@ -204,6 +230,13 @@ class Trainer:
         self.cam_positions = [(-torch.matmul(v["R"].T, v["T"])).reshape(3).contiguous()
                               for v in self.views]
         self.g_opacity = torch.zeros(scene.N, device=device, dtype=torch.float32)
+
+    def _update(self) -> None:
+        """Batch-mean gradients across ranks, then Adam. The sharded step does both (and the
+        statistic reductions) in its one kernel; otherwise reduce_step + the optimizer."""
+        if self.sharded is None:
+            reduce_step(self.fg, len(self.views), self.world, self.group)
+        self.opt.step()
 
     def step(self, targets=None, before_view=None) -> torch.Tensor:
         if self.mode == "direct":
@@ -248,8 +281,7 @@ class Trainer:
                 total += loss
             # d loss / d logit = d loss / d opacity * sigmoid'(logit), once per step
             g.alpha.grad.view(-1).addcmul_(self.g_opacity, opacity * (1.0 - opacity))
-        reduce_step(fg, len(self.views), self.world, self.group)
-        self.opt.step()
+        self._update()
         return total
 
     def _step_autograd(self, targets=None, before_view=None) -> torch.Tensor:
@@ -283,6 +315,5 @@ class Trainer:
             accumulate_view_stats(self.fg, RasterizeFunction.last_mean2d_grad, view["width"],
                                   view["height"])
             total = total + loss.detach()
-        reduce_step(self.fg, len(self.views), self.world, self.group)
-        self.opt.step()
+        self._update()
         return total

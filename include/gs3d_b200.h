@@ -212,6 +212,43 @@ GS_API int gs_adam_step(int n_groups, float* const* params, const long long* siz
                         void* stream);
 
 /*
+ * The multi-GPU optimizer step of the view-parallel training step (no counterpart in the
+ * reference, which trains on one GPU): reduce-scatter of the gradient bucket, Adam on this
+ * rank's shard, all-gather of the parameters, SUM / MAX reductions of the densification
+ * statistics, in one kernel per rank over NVLink. Every rank calls it with the same layout;
+ * the buffers are symmetric (same size on every rank, mapped into every peer). With the *_mc
+ * multicast pointers (NVSwitch) the reductions and broadcasts run as multimem operations in
+ * the switch; otherwise the *_peers device arrays (one pointer per rank) are used for peer
+ * loads and stores. Rank r owns elements [r * shard, (r + 1) * shard) of bucket and params:
+ * gradients at [0, n_param) (parameter groups of group_sizes, learning rates lrs, gradient
+ * scaled by grad_scale), SUM-reduced statistics at [stats_offset, stats_offset + n_stats), and
+ * elements [r * max_shard, ...) of the MAX-reduced statistic (n_max non-negative floats).
+ * exp_avg / exp_avg_sq hold this rank's shard of the Adam moments (shard floats each).
+ * signal_pads is a device array of each rank's signal pad (signal_slots zeroed uint32 words);
+ * barrier waits are bounded and a timeout sets a device error bit (gs_device_error_bits).
+ */
+typedef struct gs_shard_buffers {
+  int world, rank;
+  long long shard, n_param, stats_offset, n_stats, max_shard, n_max;
+  float* bucket;
+  float* bucket_mc;
+  void* const* bucket_peers;
+  float* params;
+  float* params_mc;
+  void* const* params_peers;
+  float* maxbuf;
+  float* max_mc;
+  void* const* max_peers;
+  void* const* signal_pads;
+  long long signal_slots;
+} gs_shard_buffers;
+
+GS_API int gs_sharded_adam_step(const gs_shard_buffers* buffers, float* exp_avg,
+                                float* exp_avg_sq, int n_groups, const long long* group_sizes,
+                                const float* lrs, double beta1, double beta2, double eps,
+                                long long step, float grad_scale, void* stream);
+
+/*
  * CUDA event helpers for m_ready_event (cudaEvent_t values passed as void*): create an event
  * with timing disabled, block the calling thread until it completes, destroy it.
  */

@@ -114,3 +114,22 @@ def test_failed_rank_surfaces_as_error_not_hang():
             p.kill()
     assert got[1].startswith("error")
     assert got[0].startswith("error"), "the surviving rank must see the failure, not hang"
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+@pytest.mark.parametrize("n_gaussians", [1, 5, 60_001])
+def test_shard_layout_covers_the_bucket(world, n_gaussians):
+    """Each rank's shard is a multiple of 4 elements, the shards tile the padded bucket, and the
+    statistics start 16-byte aligned after the gradients."""
+    import sys
+
+    sys.path[:0] = [os.path.join(os.path.dirname(__file__), "..", "custom-3dgs-cuda_b200")]
+    from gs3d_b200.sharded import shard_layout
+
+    n_param = 59 * n_gaussians
+    lay = shard_layout(n_param, n_gaussians, world)
+    assert lay.shard % 4 == 0 and lay.stats_offset % 4 == 0
+    assert lay.stats_offset >= n_param and lay.stats_offset - n_param < 4
+    assert lay.length == lay.shard * world >= lay.stats_offset + lay.n_stats
+    assert lay.length - (lay.stats_offset + lay.n_stats) < 4 * world + 4
+    assert lay.max_length == lay.max_shard * world >= n_gaussians
