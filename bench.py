@@ -55,6 +55,68 @@ def peaks() -> dict:
 
 
 # ---- clocks sampled during the timed region ------------------------------------------------
+class NvmlClockSampler:
+    """SM clock and clock-event reasons of one GPU sampled every 5 ms through NVML (the data
+    `nvidia-smi --query-gpu=clocks.sm,...` prints) on a host thread while the timed region runs;
+    short regions (a few ms per step at 8 GPUs) still get tens of samples."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+
+    def __init__(self, index: int):
+        import threading
+
+        import pynvml
+
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(index).uuid)
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        self.samples, self.reasons = [], set()
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            self.samples.append(float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)))
+            bits = get_reasons(self.handle)
+            for name, const in self.REASONS:
+                if bits & getattr(nv, const, 0):
+                    self.reasons.add(name)
+            self._stop.wait(0.005)
+
+    def start(self) -> None:
+        self._thread.start()
+        while not self.samples:  # the first sample precedes the timed region's start
+            time.sleep(0.001)
+
+    def stop(self) -> dict | None:
+        self._stop.set()
+        self._thread.join(timeout=5)
+        if not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
+
+
+def clock_sampler(index: int):
+    try:
+        return NvmlClockSampler(index)
+    except Exception:
+        return ClockSampler(index)
+
+
 class ClockSampler:
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -320,10 +382,23 @@ def run_reference(args, rank, world):
                              "sample": res["sample"]},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# Where the JSON line goes: the process's original stdout. main() points file descriptor 1 at
+# stderr so that library banners (NCCL's version line, for one) cannot precede the line.
+OUT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    print(json.dumps(line), file=OUT, flush=True)
 
 
 def main() -> int:
+    global OUT
+    sys.stdout.flush()
+    OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -378,9 +453,9 @@ def run_view(args) -> int:
     timer.remove()
     if _lib.device_error_bits() != 0:
         raise RuntimeError(f"device error bits {_lib.device_error_bits():#x}")
-    print(json.dumps({"mode": "view", "workload": "config2 view 0: 1M Gaussians, 1920x1080",
-                      "steps": args.steps, "warmup": args.warmup, "pairs": st.pairs,
-                      "stage_ms": timer.stage_ms()}), flush=True)
+    emit({"mode": "view", "workload": "config2 view 0: 1M Gaussians, 1920x1080",
+          "steps": args.steps, "warmup": args.warmup, "pairs": st.pairs,
+          "stage_ms": timer.stage_ms()})
     return 0
 
 
@@ -402,8 +477,22 @@ def run_ours(args, rank, world, local) -> int:
     torch.cuda.synchronize()
 
     # ---- timed region: targets resident in HBM ----
-    sampler = ClockSampler(local)
+    sampler = clock_sampler(local)
     timer = StageTimer(args.steps * len(mine))
+    # CUDA events around each step's optimizer update (gradient reduction across ranks + Adam)
+    update_events = []
+    plain_update = trainer._update
+
+    def timed_update():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        plain_update()
+        b.record()
+        update_events.append((a, b))
+
+    trainer._update = timed_update
+    if trainer.sharded is not None:
+        trainer.sharded.record_phases(args.steps)
     barrier(world)
     torch.cuda.synchronize()
     sampler.start()
@@ -416,6 +505,12 @@ def run_ours(args, rank, world, local) -> int:
     torch.cuda.synchronize()
     barrier(world)
     timer.remove()
+    trainer._update = plain_update
+    update_ms = statistics.mean(a.elapsed_time(b) for a, b in update_events)
+    update_phases = None
+    if trainer.sharded is not None:
+        update_phases = trainer.sharded.phase_ms()
+        trainer.sharded.record_phases(0)
     launches = crc.kernel_launches() - launches0
     clocks = sampler.stop()
     stage_ms = timer.stage_ms()
@@ -473,6 +568,12 @@ def run_ours(args, rank, world, local) -> int:
                    "l2": "inputs larger than L2 (236 MB of parameters + 25 MB per target)"},
         "per_view_config2": breakdown,
         "stage_ms_per_view": stage_ms,
+        "update_ms_per_step": update_ms,
+        "update_phases_ms_rank0": update_phases,
+        "update": ("fused reduce-scatter + sharded Adam + all-gather (multicast)"
+                   if trainer.sharded is not None and trainer.sharded.multicast else
+                   "fused reduce-scatter + sharded Adam + all-gather (peer memory)"
+                   if trainer.sharded is not None else "single-launch Adam"),
         "views_pairs": stats,
         "gpu_launches": total_launches,
         "gpu_launches_per_rank": launches,
@@ -484,7 +585,7 @@ def run_ours(args, rank, world, local) -> int:
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(sc, sc.views[0], targets[0])
         line["cpu_baseline"].pop("seconds", None)
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 

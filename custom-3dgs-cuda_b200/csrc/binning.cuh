@@ -154,6 +154,8 @@ static __global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinPara
 struct DupParams {
   int tiles_x;
   int n_tile_passes;
+  int tile_shift[4];      // digit bit offset of each tile-sort pass
+  unsigned tile_mask[4];  // digit mask of each tile-sort pass
   const int* n_visible;
   const int* pair_count;
   long long pair_capacity;
@@ -231,8 +233,10 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
     const unsigned tile_id = (unsigned)(r.y0 + row) * (unsigned)p.tiles_x + (unsigned)r.x0 + col;
     p.tile_keys[base + q] = tile_id;
     p.tile_vals[base + q] = s_gid[lo];
-    for (int pass = 0; pass < p.n_tile_passes; ++pass)
-      atomicAdd(&s_hist[pass][(tile_id >> (8 * pass)) & 255u], 1u);
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass)  // constant indices keep the parameters in registers
+      if (pass < p.n_tile_passes)
+        atomicAdd(&s_hist[pass][(tile_id >> p.tile_shift[pass]) & p.tile_mask[pass]], 1u);
   }
   __syncthreads();
   for (int k = tid; k < p.n_tile_passes * 256; k += kBinThreads) {

@@ -1,5 +1,5 @@
 // One pass of a stable least-significant-digit radix sort of (u32 key, u32 value) pairs
-// with 8-bit digits, after Adinets & Merrill, "Onesweep: A Faster Least Significant Digit
+// with digits of up to 8 bits, after Adinets & Merrill, "Onesweep: A Faster Least Significant Digit
 // Radix Sort for GPUs" (2022): a single kernel per digit that ranks a tile of items with
 // warp-level multi-split, publishes per-digit tile counts and resolves each tile's global
 // offset with a decoupled look-back over its predecessors, then scatters through shared
@@ -28,9 +28,10 @@ struct SortPass {
   unsigned* status;            // look-back words [tiles][256], zeroed before the sort
   unsigned* ticket;            // tile ticket counter, zeroed before the sort
   int shift;                   // bit offset of this pass's digit
+  unsigned mask;               // digit mask: (1 << digit bits) - 1, at most 255
 };
 
-static __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(SortPass a) {
+static __global__ void __launch_bounds__(kSortThreads, 3) onesweep_pass_kernel(SortPass a) {
   __shared__ unsigned s_tile;
   __shared__ unsigned s_warp_hist[kSortWarps][kRadix];
   __shared__ unsigned s_local_start[kRadix];
@@ -68,7 +69,7 @@ static __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(Sort
   for (int j = 0; j < kSortItems; ++j) {
     const int idx = warp_base + j * 32 + lane;
     const bool valid = idx < n;
-    const unsigned d = valid ? ((keys[j] >> a.shift) & (kRadix - 1)) : (unsigned)kRadix;
+    const unsigned d = valid ? ((keys[j] >> a.shift) & a.mask) : (unsigned)kRadix;
     const unsigned peers = __match_any_sync(0xffffffffu, d);
     const unsigned lower = __popc(peers & lt);
     const unsigned cnt = valid ? wh[d] : 0u;
@@ -88,15 +89,19 @@ static __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(Sort
     s_warp_hist[w][d] = tile_count;
     tile_count += c;
   }
+  // a digit absent from the whole input has prefix 0 in every tile: published as final at
+  // once, and no look-back runs for it
+  const unsigned digit_total = __ldg(a.digit_hist + d);
   unsigned* my_status = a.status + (size_t)tile * kRadix + d;
-  st_relaxed(my_status, (tile == 0 ? kFlagPrefix : kFlagAggregate) | tile_count);
+  st_relaxed(my_status,
+             (tile == 0 || digit_total == 0u ? kFlagPrefix : kFlagAggregate) | tile_count);
 
   unsigned tile_total;
   const unsigned local_start = block_exclusive_scan(tile_count, s_scan, &tile_total);
   unsigned hist_total;
-  const unsigned digit_base = block_exclusive_scan(__ldg(a.digit_hist + d), s_scan, &hist_total);
+  const unsigned digit_base = block_exclusive_scan(digit_total, s_scan, &hist_total);
   unsigned excl = 0;
-  if (tile > 0) {
+  if (tile > 0 && digit_total != 0u) {
     excl = lookback_serial(a.status + d, tile, kRadix);
     st_relaxed(my_status, kFlagPrefix | (excl + tile_count));
   }
@@ -109,7 +114,7 @@ static __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(Sort
   for (int j = 0; j < kSortItems; ++j) {
     const int idx = warp_base + j * 32 + lane;
     if (idx < n) {
-      const unsigned dj = (keys[j] >> a.shift) & (kRadix - 1);
+      const unsigned dj = (keys[j] >> a.shift) & a.mask;
       const unsigned pos = s_local_start[dj] + wh[dj] + rank[j];
       s_keys[pos] = keys[j];
       s_vals[pos] = vals[j];
@@ -119,7 +124,7 @@ static __global__ void __launch_bounds__(kSortThreads) onesweep_pass_kernel(Sort
   const int count = min(kSortTileItems, n - tile * kSortTileItems);
   for (int i = tid; i < count; i += kSortThreads) {
     const unsigned k = s_keys[i];
-    const unsigned gpos = s_global_off[(k >> a.shift) & (kRadix - 1)] + i;
+    const unsigned gpos = s_global_off[(k >> a.shift) & a.mask] + i;
     if (gpos >= (unsigned)n) {  // only reachable after a look-back timeout
       raise_device_error(kErrBadIndex);
       continue;

@@ -29,10 +29,10 @@ __global__ void __launch_bounds__(256) build_records_kernel(int N, const float* 
                                    __int_as_float(i));
 }
 
-static int tile_sort_passes(long long T) {
+static int tile_id_bits(long long T) {
   int bits = 0;
   while (bits < 32 && ((T - 1) >> bits) > 0) ++bits;
-  return (bits + 7) / 8;
+  return bits;
 }
 
 RasterLayout make_raster_layout(int N, int W, int H, long long capacity) {
@@ -40,7 +40,14 @@ RasterLayout make_raster_layout(int N, int W, int H, long long capacity) {
   L.tiles_x = (W + kTileSide - 1) / kTileSide;
   L.tiles_y = (H + kTileSide - 1) / kTileSide;
   L.T = (long long)L.tiles_x * L.tiles_y;
-  L.tile_passes = tile_sort_passes(L.T);
+  const int bits = tile_id_bits(L.T);
+  L.tile_passes = (bits + 7) / 8;
+  for (int p = 0, shift = 0; p < L.tile_passes; ++p) {
+    const int w = std::min(8, bits - shift);  // 8-bit digits, the remainder last
+    L.tile_shift[p] = shift;
+    L.tile_mask[p] = (1u << w) - 1u;
+    shift += w;
+  }
   const long long nb = ((long long)N + kBinThreads - 1) / kBinThreads;
   const long long nd = ((long long)N + kSortTileItems - 1) / kSortTileItems;
   const long long nt = (capacity + kSortTileItems - 1) / kSortTileItems;
@@ -144,6 +151,7 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
       sp.status = reinterpret_cast<unsigned*>(ws + L.status_depth) + (size_t)pass * L.nd * 256;
       sp.ticket = &hdr->ticket_depth[pass];
       sp.shift = 8 * pass;
+      sp.mask = 255u;
       onesweep_pass_kernel<<<(unsigned)L.nd, kSortThreads, 0, stream>>>(sp);
       GS_CHECK_LAUNCH();
     }
@@ -151,6 +159,10 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
     DupParams dp;
     dp.tiles_x = L.tiles_x;
     dp.n_tile_passes = P;
+    for (int k = 0; k < 4; ++k) {
+      dp.tile_shift[k] = L.tile_shift[k];
+      dp.tile_mask[k] = L.tile_mask[k];
+    }
     dp.n_visible = &hdr->n_visible;
     dp.pair_count = &hdr->pair_count;
     dp.pair_capacity = capacity;
@@ -176,7 +188,8 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
       sp.digit_hist = reinterpret_cast<unsigned*>(ws + L.tile_hist) + pass * 256;
       sp.status = reinterpret_cast<unsigned*>(ws + L.status_tile) + (size_t)pass * L.nt * 256;
       sp.ticket = &hdr->ticket_tile[pass];
-      sp.shift = 8 * pass;
+      sp.shift = L.tile_shift[pass];
+      sp.mask = L.tile_mask[pass];
       if (L.nt > 0) {
         onesweep_pass_kernel<<<(unsigned)L.nt, kSortThreads, 0, stream>>>(sp);
         GS_CHECK_LAUNCH();

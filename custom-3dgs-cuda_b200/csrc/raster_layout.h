@@ -18,6 +18,10 @@ struct RasterHeader {
 
 struct RasterLayout {
   int tiles_x = 0, tiles_y = 0, tile_passes = 0;
+  // digit of each tile-sort pass: 8 bits, the remainder of the tile-id bits in the last pass
+  // (an even split, 7 + 6 at 1080p, measured slower: fewer histogram bins contend more)
+  int tile_shift[4] = {0, 0, 0, 0};
+  unsigned tile_mask[4] = {0u, 0u, 0u, 0u};
   long long T = 0, nb = 0, nd = 0, nt = 0;
   size_t header = 0, depth_hist = 0, tile_hist = 0, status_dup = 0,
          status_depth = 0, status_tile = 0, zero_bytes = 0;

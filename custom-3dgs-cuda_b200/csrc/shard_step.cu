@@ -28,6 +28,7 @@ namespace gs {
 constexpr int kShardThreads = 256;
 constexpr int kShardMaxGroups = 8;
 constexpr int kShardMaxWorld = 8;
+constexpr int kShardUnroll = 4;
 
 struct ShardArgs {
   gs_shard_buffers b;
@@ -147,52 +148,78 @@ __device__ __forceinline__ void adam_lane(const ShardArgs& a, long long idx, flo
   p -= a.step_size[grp] * (m / denom);
 }
 
+__device__ __forceinline__ void mark_phase(const gs_shard_buffers& b, int k) {
+  if (b.phase_ns && threadIdx.x == 0) {
+    const unsigned long long t = global_ns();
+    if (k == 0)
+      atomicMin(b.phase_ns, t);
+    else
+      atomicMax(b.phase_ns + k, t);
+  }
+}
+
 template <bool kMulticast>
 __global__ void __launch_bounds__(kShardThreads) sharded_adam_kernel(ShardArgs a) {
   const gs_shard_buffers& b = a.b;
+  mark_phase(b, 0);
   if (!peer_barrier(a)) return;
+  mark_phase(b, 1);
   fence_proxy_alias();
   const long long lo = (long long)b.rank * b.shard, hi = lo + b.shard;
+  const long long data_end = min(hi, b.stats_offset + b.n_stats);
   const long long stride = 4ll * gridDim.x * blockDim.x;
-  for (long long i = lo + 4ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
-       i += stride) {
-    const bool is_param = i < b.stats_offset;
-    const bool is_stat = i >= b.stats_offset && i < b.stats_offset + b.n_stats;
-    if (!is_param && !is_stat) continue;
-    float4 g;
-    if (kMulticast) {
-      g = mm_ld_reduce_add_v4(b.bucket_mc + i);
-    } else {
-      g = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < b.world; ++r) {
-        const float4 x = *reinterpret_cast<const float4*>(
-            static_cast<const float*>(b.bucket_peers[r]) + i);
-        g.x += x.x;
-        g.y += x.y;
-        g.z += x.z;
-        g.w += x.w;
+  // kShardUnroll 16-byte groups per thread and iteration: all reductions are issued before the
+  // first update so that several NVLink round trips are in flight per thread
+  for (long long i0 = lo + 4ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+       i0 < data_end; i0 += kShardUnroll * stride) {
+    float4 g[kShardUnroll], pp[kShardUnroll], mm[kShardUnroll], vv[kShardUnroll];
+#pragma unroll
+    for (int u = 0; u < kShardUnroll; ++u) {
+      const long long i = i0 + u * stride;
+      g[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i >= data_end) continue;
+      if (i < b.stats_offset) {  // this rank's parameters and moments, loaded alongside
+        pp[u] = *reinterpret_cast<const float4*>(b.params + i);
+        mm[u] = *reinterpret_cast<const float4*>(a.exp_avg + (i - lo));
+        vv[u] = *reinterpret_cast<const float4*>(a.exp_avg_sq + (i - lo));
+      }
+      if (kMulticast) {
+        g[u] = mm_ld_reduce_add_v4(b.bucket_mc + i);
+      } else {
+        for (int r = 0; r < b.world; ++r) {
+          const float4 x = *reinterpret_cast<const float4*>(
+              static_cast<const float*>(b.bucket_peers[r]) + i);
+          g[u].x += x.x;
+          g[u].y += x.y;
+          g[u].z += x.z;
+          g[u].w += x.w;
+        }
       }
     }
-    float4 out = g;
-    if (is_param) {
-      float4 p = *reinterpret_cast<const float4*>(b.params + i);
-      float4 m = *reinterpret_cast<const float4*>(a.exp_avg + (i - lo));
-      float4 v = *reinterpret_cast<const float4*>(a.exp_avg_sq + (i - lo));
-      if (i + 0 < b.n_param) adam_lane(a, i + 0, g.x, p.x, m.x, v.x);
-      if (i + 1 < b.n_param) adam_lane(a, i + 1, g.y, p.y, m.y, v.y);
-      if (i + 2 < b.n_param) adam_lane(a, i + 2, g.z, p.z, m.z, v.z);
-      if (i + 3 < b.n_param) adam_lane(a, i + 3, g.w, p.w, m.w, v.w);
-      *reinterpret_cast<float4*>(a.exp_avg + (i - lo)) = m;
-      *reinterpret_cast<float4*>(a.exp_avg_sq + (i - lo)) = v;
-      out = p;
-    }
-    float* dst_mc = is_param ? b.params_mc : b.bucket_mc;
-    void* const* dst_peers = is_param ? b.params_peers : b.bucket_peers;
-    if (kMulticast) {
-      mm_st_v4(dst_mc + i, out);
-    } else {
-      for (int r = 0; r < b.world; ++r)
-        *reinterpret_cast<float4*>(static_cast<float*>(dst_peers[r]) + i) = out;
+#pragma unroll
+    for (int u = 0; u < kShardUnroll; ++u) {
+      const long long i = i0 + u * stride;
+      if (i >= data_end) continue;
+      const bool is_param = i < b.stats_offset;
+      float4 out = g[u];
+      if (is_param) {
+        float4 p = pp[u], m = mm[u], v = vv[u];
+        if (i + 0 < b.n_param) adam_lane(a, i + 0, g[u].x, p.x, m.x, v.x);
+        if (i + 1 < b.n_param) adam_lane(a, i + 1, g[u].y, p.y, m.y, v.y);
+        if (i + 2 < b.n_param) adam_lane(a, i + 2, g[u].z, p.z, m.z, v.z);
+        if (i + 3 < b.n_param) adam_lane(a, i + 3, g[u].w, p.w, m.w, v.w);
+        *reinterpret_cast<float4*>(a.exp_avg + (i - lo)) = m;
+        *reinterpret_cast<float4*>(a.exp_avg_sq + (i - lo)) = v;
+        out = p;
+      }
+      float* dst_mc = is_param ? b.params_mc : b.bucket_mc;
+      void* const* dst_peers = is_param ? b.params_peers : b.bucket_peers;
+      if (kMulticast) {
+        mm_st_v4(dst_mc + i, out);
+      } else {
+        for (int r = 0; r < b.world; ++r)
+          *reinterpret_cast<float4*>(static_cast<float*>(dst_peers[r]) + i) = out;
+      }
     }
   }
   // max statistic
@@ -212,7 +239,9 @@ __global__ void __launch_bounds__(kShardThreads) sharded_adam_kernel(ShardArgs a
     }
   }
   fence_proxy_alias();
+  mark_phase(b, 2);
   peer_barrier(a);
+  mark_phase(b, 3);
   fence_proxy_alias();
 }
 

@@ -59,7 +59,8 @@ class ShardBuffers(ctypes.Structure):
                 ("bucket", c_void_p), ("bucket_mc", c_void_p), ("bucket_peers", c_void_p),
                 ("params", c_void_p), ("params_mc", c_void_p), ("params_peers", c_void_p),
                 ("maxbuf", c_void_p), ("max_mc", c_void_p), ("max_peers", c_void_p),
-                ("signal_pads", c_void_p), ("signal_slots", c_longlong)]
+                ("signal_pads", c_void_p), ("signal_slots", c_longlong),
+                ("phase_ns", c_void_p)]
 
 
 class ShardedStep:
@@ -167,7 +168,33 @@ class ShardedStep:
         o = self.layout.stats_offset + n
         return self.bucket[o:o + n]
 
+    def record_phases(self, steps: int) -> None:
+        """Record the kernel phases (kernel start, end of the opening barrier, of the data loop,
+        of the closing barrier; globaltimer ns) of the next `steps` steps; 0 turns it off. The
+        rows are allocated and initialised here, so recording adds no host-device copy."""
+        self.desc.phase_ns = None
+        self._phase_rows = None
+        self._phase_used = 0
+        if steps > 0:
+            init = torch.tensor([-1, 0, 0, 0], dtype=torch.int64)
+            self._phase_rows = init.repeat(steps, 1).to(self.device)
+
+    def phase_ms(self) -> dict | None:
+        """Mean per-step phase durations (ms) of the recorded steps."""
+        if self._phase_rows is None or self._phase_used == 0:
+            return None
+        p = self._phase_rows[:self._phase_used].cpu().to(torch.float64)
+        d = (p[:, 1:] - p[:, :-1]) * 1e-6
+        return {"opening_barrier": float(d[:, 0].mean()), "data": float(d[:, 1].mean()),
+                "closing_barrier": float(d[:, 2].mean())}
+
     def step(self) -> None:
+        rows = getattr(self, "_phase_rows", None)
+        if rows is not None and self._phase_used < rows.shape[0]:
+            self.desc.phase_ns = rows[self._phase_used].data_ptr()
+            self._phase_used += 1
+        else:
+            self.desc.phase_ns = None
         self.n_steps += 1
         k = len(self.param_groups)
         lrs = (ctypes.c_float * k)(*[g["lr"] for g in self.param_groups])

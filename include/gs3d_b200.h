@@ -241,6 +241,10 @@ typedef struct gs_shard_buffers {
   void* const* max_peers;
   void* const* signal_pads;
   long long signal_slots;
+  /* optional (may be NULL): 4 device words that receive, in globaltimer nanoseconds, the
+     earliest CTA start, the latest end of the opening barrier, of the data loop and of the
+     closing barrier (initialise to {~0, 0, 0, 0}) */
+  unsigned long long* phase_ns;
 } gs_shard_buffers;
 
 GS_API int gs_sharded_adam_step(const gs_shard_buffers* buffers, float* exp_avg,
