@@ -406,6 +406,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--view-streams", type=int, default=3,
+                    help="CUDA streams the views of a step alternate over (1 = in order)")
     ap.add_argument("--view-only", action="store_true",
                     help="forward+backward of one config-2 view per step (single GPU); a small "
                          "fixed workload for profiler captures of single kernels")
@@ -467,7 +469,8 @@ def run_ours(args, rank, world, local) -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     sc, targets = scenes.config4(0, n=args.gaussians, n_views=BATCH_VIEWS)
-    trainer = Trainer(sc, sc.views, [t.to(dev) for t in targets], dev, rank, world)
+    trainer = Trainer(sc, sc.views, [t.to(dev) for t in targets], dev, rank, world,
+                      view_streams=args.view_streams)
     mine = trainer.plan.views()
     host_targets = {vi: targets[vi].pin_memory() for vi in mine}
     h2d_bytes = sum(host_targets[vi].numel() * 4 for vi in mine)
@@ -478,7 +481,6 @@ def run_ours(args, rank, world, local) -> int:
 
     # ---- timed region: targets resident in HBM ----
     sampler = clock_sampler(local)
-    timer = StageTimer(args.steps * len(mine))
     # CUDA events around each step's optimizer update (gradient reduction across ranks + Adam)
     update_events = []
     plain_update = trainer._update
@@ -500,11 +502,10 @@ def run_ours(args, rank, world, local) -> int:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        trainer.step(before_view=lambda vi: timer.install_next())
+        trainer.step()
     e1.record()
     torch.cuda.synchronize()
     barrier(world)
-    timer.remove()
     trainer._update = plain_update
     update_ms = statistics.mean(a.elapsed_time(b) for a, b in update_events)
     update_phases = None
@@ -513,8 +514,17 @@ def run_ours(args, rank, world, local) -> int:
         trainer.sharded.record_phases(0)
     launches = crc.kernel_launches() - launches0
     clocks = sampler.stop()
-    stage_ms = timer.stage_ms()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1), world)
+
+    # ---- per-stage library timings (untimed steps, views in order on one stream, so that each
+    # stage's events bracket only its own kernels) ----
+    stage_steps = min(args.steps, 5)
+    timer = StageTimer(stage_steps * len(mine))
+    for _ in range(stage_steps):
+        trainer.step(before_view=lambda vi: timer.install_next())
+    torch.cuda.synchronize()
+    timer.remove()
+    stage_ms = timer.stage_ms()
     total_launches = int(sum_over_ranks(float(launches), world))
 
     # ---- e2e: every step copies its targets from pinned host memory (side stream, each view's
@@ -568,6 +578,7 @@ def run_ours(args, rank, world, local) -> int:
                    "l2": "inputs larger than L2 (236 MB of parameters + 25 MB per target)"},
         "per_view_config2": breakdown,
         "stage_ms_per_view": stage_ms,
+        "view_streams": len(trainer._streams) or 1,
         "update_ms_per_step": update_ms,
         "update_phases_ms_rank0": update_phases,
         "update": ("fused reduce-scatter + sharded Adam + all-gather (multicast)"

@@ -301,7 +301,8 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
                                   float* g_opacity, float* g_albedo, float* g_k_j,
                                   float* g_mean2d, int accumulate, float* stat_norm_sum,
                                   float* stat_count, float* stat_max, float stat_scale_x,
-                                  float stat_scale_y, void* stream) {
+                                  float stat_scale_y, void* accum_wait_event,
+                                  void* accum_done_event, void* stream) {
   GS_API_BEGIN();
   GS_REQUIRE(N >= 0, "N must be non-negative");
   GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
@@ -375,8 +376,12 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
                                (int)kPreprocessSmem));
   GS_CUDA(cudaFuncSetAttribute(render_gaussian_backward_kernel,
                                cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+  // the only kernel of the backward that writes the caller's gradient / statistic buffers:
+  // ordered after accum_wait_event so that views rendered on other streams can share them
+  if (accum_wait_event) GS_CUDA(cudaStreamWaitEvent(st, (cudaEvent_t)accum_wait_event, 0));
   render_gaussian_backward_kernel<<<(N + 255) / 256, 256, kPreprocessSmem, st>>>(gp);
   GS_CHECK_LAUNCH();
+  if (accum_done_event) GS_CUDA(cudaEventRecord((cudaEvent_t)accum_done_event, st));
   mark_stage(9, st);
   return GS_OK;
   GS_API_END();

@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
     }
     const int gx = bx + col;
     const size_t HW = (size_t)H * W;
+    float run_sum = 0.f;  // at most 8 terms in [-1, 1]; summed in double across runs
 #pragma unroll
     for (int o = 0; o < kSsimRun; ++o) {
       const int gy = by + rb * kSsimRun + o;
@@ -175,18 +176,20 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
       const float vx = m[2][o] - mx * mx, vy = m[3][o] - my * my, cxy = m[4][o] - mx * my;
       const float n1 = 2.f * mx * my + kSsimC1, n2 = 2.f * cxy + kSsimC2;
       const float d1 = mx * mx + my * my + kSsimC1, d2 = vx + vy + kSsimC2;
-      const float den = d1 * d2;
-      const float S = (n1 * n2) / den;
-      const float B = -S / d2;
-      const float Cm = 2.f * n1 / den;
-      const float dmx = (2.f * my * n2) / den - S * (2.f * mx) / d1;
+      // one reciprocal: 1/den, 1/d1 = d2/den, 1/d2 = d1/den
+      const float r = 1.0f / (d1 * d2);
+      const float S = n1 * n2 * r;
+      const float B = -S * (d1 * r);
+      const float Cm = 2.f * n1 * r;
+      const float dmx = 2.f * my * n2 * r - 2.f * mx * S * (d2 * r);
       const float A = dmx - 2.f * mx * B - my * Cm;
       const size_t pix = (size_t)gy * W + gx;
       maps[(0 + c) * HW + pix] = A;
       maps[(3 + c) * HW + pix] = B;
       maps[(6 + c) * HW + pix] = Cm;
-      ssim_sum += (double)S;
+      run_sum += S;
     }
+    ssim_sum += (double)run_sum;
   }
   // block reduction in a fixed order
 #pragma unroll

@@ -69,11 +69,13 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
 
 
 def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, cam_pos, fx, fy,
-                    cx, cy, want_mean2d_grad: bool = True, out=None, stats=None):
+                    cx, cy, want_mean2d_grad: bool = True, out=None, stats=None,
+                    accum_wait=None, accum_done=None):
     """Gradients (mu, q, s, opacity[N], albedo, k_j, mean2d or None). With `out` (a tuple of
     the first six buffers) the gradients are added into those buffers instead. `stats` =
     (norm_sum[N], count[N], norm_max[N], scale_x, scale_y) updates the densification
-    statistics in the same pass."""
+    statistics in the same pass. `accum_wait` / `accum_done` (`_lib.Event` or None) order the
+    kernel that writes `out` and `stats` after / before other streams' writes to them."""
     N = int(mu.shape[0])
     dev = mu.device
     f32 = dict(device=dev, dtype=torch.float32)
@@ -96,5 +98,7 @@ def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, c
             _ptr(g_mean2d), 1 if accumulate else 0,
             *((_ptr(stats[0]), _ptr(stats[1]), _ptr(stats[2]), float(stats[3]), float(stats[4]))
               if stats is not None else (None, None, None, 0.0, 0.0)),
+            accum_wait.handle if accum_wait is not None else None,
+            accum_done.handle if accum_done is not None else None,
             _stream(dev)))
     return (*out, g_mean2d)

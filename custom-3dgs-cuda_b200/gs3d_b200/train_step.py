@@ -176,13 +176,15 @@ class Trainer:
     mode "direct" (default) calls the fused render and loss kernels without autograd: each
     view's parameter gradients are added straight into the flat bucket, the densification
     statistics are updated inside the per-Gaussian backward kernel and the opacity gradient is
-    taken through the sigmoid once per step. mode "autograd" runs the same step through
+    taken through the sigmoid once per step. Consecutive views run on `view_streams`
+    alternating CUDA streams (1 = all on the current stream). mode "autograd" runs the same step through
     `gaussian_splatting.rasterizer.rasterize` (the drop-in RasterizeFunction) and
     loss.backward(), as the reference trainer does.
     """
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
-                 fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct"):
+                 fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct",
+                 view_streams: int = 3):
         from gaussian_splatting.scene.gaussian import gaussian
 
         self.device = device
@@ -230,6 +232,13 @@ class Trainer:
         self.cam_positions = [(-torch.matmul(v["R"].T, v["T"])).reshape(3).contiguous()
                               for v in self.views]
         self.g_opacity = torch.zeros(scene.N, device=device, dtype=torch.float32)
+        self._streams, self._accum_events = [], []
+        if mode == "direct" and device.type == "cuda" and view_streams > 1:
+            from custom_rasterizer_cuda import _lib
+
+            with torch.cuda.device(device):
+                self._streams = [torch.cuda.Stream(device) for _ in range(view_streams)]
+                self._accum_events = [_lib.Event(), _lib.Event()]
 
     def _update(self) -> None:
         """Batch-mean gradients across ranks, then Adam. The sharded step does both (and the
@@ -261,24 +270,43 @@ class Trainer:
             mu, q, s, A, kj = g.mu.detach(), g.q.detach(), g.s.detach(), g.A.detach(), g.k_j.detach()
             opacity = torch.sigmoid(g.alpha.detach()).reshape(-1)
             out = (g.mu.grad, g.q.grad, g.s.grad, self.g_opacity, g.A.grad, g.k_j.grad)
-            total = torch.zeros((), device=self.device)
-            for vi in self.plan.views():
+            main = torch.cuda.current_stream(self.device)
+            # consecutive views on alternating streams (unless a per-view hook wants them in
+            # order): a view's forward overlaps the previous view's loss and backward; only the
+            # kernels that add into the shared gradient bucket are chained across streams
+            streams = self._streams if (self._streams and before_view is None) else [main]
+            for st in streams:
+                if st is not main:
+                    st.wait_stream(main)
+            losses, prev_done = [], None
+            for k, vi in enumerate(self.plan.views()):
                 v = self.views[vi]
                 cam = self.cam_positions[vi]
                 if before_view is not None:
                     before_view(vi)
-                img, _, st = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
-                                            v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
-                                            v["width"])
-                target = targets.get(vi) if staged else targets[vi]
-                loss, gimg = l1_ssim_value_and_grad(img, target, LAMBDA_DSSIM)
-                if staged:
-                    targets.release(vi)
-                render_backward(st, gimg, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
-                                v["cx"], v["cy"], want_mean2d_grad=False, out=out,
-                                stats=(fg.grad_norm_sum, fg.grad_count, fg.max_grad,
-                                       v["width"] / 2.0, v["height"] / 2.0))
-                total += loss
+                st = streams[k % len(streams)]
+                done = self._accum_events[k % 2] if len(streams) > 1 else None
+                with torch.cuda.stream(st):
+                    img, _, rs = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
+                                                v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
+                                                v["width"])
+                    target = targets.get(vi) if staged else targets[vi]
+                    loss, gimg = l1_ssim_value_and_grad(img, target, LAMBDA_DSSIM)
+                    if staged:
+                        targets.release(vi)
+                    render_backward(rs, gimg, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"],
+                                    v["fy"], v["cx"], v["cy"], want_mean2d_grad=False, out=out,
+                                    stats=(fg.grad_norm_sum, fg.grad_count, fg.max_grad,
+                                           v["width"] / 2.0, v["height"] / 2.0),
+                                    accum_wait=prev_done, accum_done=done)
+                prev_done = done
+                if st is not main:
+                    loss.record_stream(main)
+                losses.append(loss)
+            for st in streams:
+                if st is not main:
+                    main.wait_stream(st)
+            total = torch.stack(losses).sum() if losses else torch.zeros((), device=self.device)
             # d loss / d logit = d loss / d opacity * sigmoid'(logit), once per step
             g.alpha.grad.view(-1).addcmul_(self.g_opacity, opacity * (1.0 - opacity))
         self._update()

@@ -155,6 +155,9 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
  * given, the reference trainer's densification statistics are updated in the same pass
  * (gaussian_splatting/utils/adc.py:58-87): n = |dL/dmean2d * (stat_scale_x, stat_scale_y)|,
  * and where n > 0, stat_norm_sum += n, stat_count += 1, stat_max = max(stat_max, n).
+ * accum_wait_event / accum_done_event (cudaEvent_t or NULL): the kernel that writes the gradient
+ * and statistic buffers waits for the first and the second is recorded after it, so that views
+ * rendered concurrently on several streams can accumulate into the same buffers.
  */
 GS_API size_t gs_render_workspace_size(int N, int H, int W, long long pair_capacity);
 GS_API int gs_render_forward(int N, int H, int W, const float* mu, const float* q, const float* s,
@@ -177,7 +180,7 @@ GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const 
                               float* g_opacity, float* g_albedo, float* g_k_j, float* g_mean2d,
                               int accumulate, float* stat_norm_sum, float* stat_count,
                               float* stat_max, float stat_scale_x, float stat_scale_y,
-                              void* stream);
+                              void* accum_wait_event, void* accum_done_event, void* stream);
 
 /*
  * Fused photometric loss of the training step (no counterpart in the reference's extension;

@@ -73,3 +73,23 @@ def test_host_staged_targets_match_resident_targets(cuda_device, mode):
         assert abs(l_r - l_s) <= 1e-6 * abs(l_r)
     for a, b in zip(resident.params, staged_tr.params):
         assert_grad_close(b.detach().cpu().numpy(), a.detach().cpu().numpy(), "parameters")
+
+
+def test_concurrent_view_streams_give_the_same_bucket(cuda_device):
+    """Views on two alternating streams (the default) give the one-stream step's loss exactly and
+    its bucket and statistics within float atomic-order rounding (the blend backward's atomics
+    are order-nondeterministic on one stream already)."""
+    from gs3d_b200.train_step import Trainer
+
+    sc, views, targets = _small_setup()
+    tg = [t.to(cuda_device) for t in targets]
+    got = {}
+    for n in (1, 2):
+        tr = Trainer(sc, views, tg, cuda_device, view_streams=n)
+        tr.opt.step = lambda: None
+        loss = tr.step()
+        torch.cuda.synchronize()
+        got[n] = (float(loss), tr.fg.buffer.cpu().clone(), tr.fg.max_grad.cpu().clone())
+    assert got[1][0] == got[2][0]
+    assert_grad_close(got[2][1].numpy(), got[1][1].numpy(), "bucket")
+    assert_grad_close(got[2][2].numpy(), got[1][2].numpy(), "max statistic")
