@@ -262,7 +262,8 @@ def per_view_breakdown(trainer, view: dict, reps: int = 5) -> dict:
 
 
 def view_pair_stats(trainer, views: list[dict]) -> dict:
-    """Pairs M and replayed (pixel, Gaussian) pairs (sum of n_contrib) of each view."""
+    """Pairs M and replayed (pixel, Gaussian) pairs (sum of n_contrib) of each view, with the
+    binning the trainer uses (with tight bins both count only the shorter lists' entries)."""
     from custom_rasterizer_cuda.render import render_forward
 
     pairs, replayed = [], []
@@ -273,7 +274,8 @@ def view_pair_stats(trainer, views: list[dict]) -> dict:
             R, t = v["R"], v["T"]
             cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
             _, _, st = render_forward(mu, q, s, op, A, kj, R, t, cam, v["fx"], v["fy"], v["cx"],
-                                      v["cy"], v["height"], v["width"])
+                                      v["cy"], v["height"], v["width"],
+                                      tight_bins=getattr(trainer, "tight_bins", False))
             pairs.append(st.pairs)
             replayed.append(int(st.n_contrib.sum().item()))
     return {"pairs": pairs, "replayed_pairs": replayed}
@@ -579,6 +581,7 @@ def run_ours(args, rank, world, local) -> int:
         "per_view_config2": breakdown,
         "stage_ms_per_view": stage_ms,
         "view_streams": len(trainer._streams) or 1,
+        "tight_bins": trainer.tight_bins,
         "update_ms_per_step": update_ms,
         "update_phases_ms_rank0": update_phases,
         "update": ("fused reduce-scatter + sharded Adam + all-gather (multicast)"

@@ -54,11 +54,15 @@ struct BinParams {
   int* n_visible;
   int* pair_count;              // M, clamped to INT_MAX
   long long pair_capacity;
+  int tight;                    // 1: intersect each rectangle with the opacity-test extent
 };
 
 // Per-Gaussian part of binning: tile rectangle and count of a projected splat; for a splat
 // covering at least one tile it also writes the packed rectangle and the blend record and
-// returns the depth key. Shared by bin_prepare_kernel and the fused render preprocess.
+// returns the depth key. Shared by bin_prepare_kernel and the fused render preprocess. With
+// p.tight the reference's rectangle is intersected with the tiles that hold a pixel of the
+// splat's opacity-test extent box: the image, transmittance and gradients are unchanged (the
+// dropped pairs fail the opacity test at every pixel of their tile), the tile lists shorter.
 __device__ __forceinline__ unsigned bin_gaussian(const BinParams& p, int i, float2 mean,
                                                  float a, float b, float c, float depth,
                                                  float3 color, float opacity,
@@ -68,10 +72,35 @@ __device__ __forceinline__ unsigned bin_gaussian(const BinParams& p, int i, floa
   depth_bits = 0;
   if (splat_tile_rect(mean, a, b, c, p.W, p.H, p.tiles_x, p.tiles_y, r)) {
     count = (unsigned)rect_count(r);
+    float3 conic;
+    float2 ext;
+    if (count > 0) {
+      conic = conic_from_cov(a, b, c);
+      ext = splat_extent(conic, opacity);
+      if (p.tight) {
+        // keep only the tiles that hold a pixel inside the extent box: every other pair of the
+        // reference's rectangle fails the opacity test at all of its tile's pixels
+        if (ext.x == -INFINITY) {
+          count = 0;
+        } else if (ext.x != INFINITY) {
+          const float lo_x = fmaxf(mean.x - ext.x, 0.0f);
+          const float hi_x = fminf(mean.x + ext.x, (float)(p.W - 1));
+          const float lo_y = fmaxf(mean.y - ext.y, 0.0f);
+          const float hi_y = fminf(mean.y + ext.y, (float)(p.H - 1));
+          if (hi_x < lo_x || hi_y < lo_y) {
+            count = 0;
+          } else {
+            r.x0 = max(r.x0, (int)ceilf(lo_x) / kTileSide);
+            r.x1 = min(r.x1, (int)floorf(hi_x) / kTileSide + 1);
+            r.y0 = max(r.y0, (int)ceilf(lo_y) / kTileSide);
+            r.y1 = min(r.y1, (int)floorf(hi_y) / kTileSide + 1);
+            count = (unsigned)rect_count(r);
+          }
+        }
+      }
+    }
     if (count > 0) {
       p.rects[i] = pack_rect(r);
-      const float3 conic = conic_from_cov(a, b, c);
-      const float2 ext = splat_extent(conic, opacity);
       p.records[3 * i + 0] = make_float4(mean.x, mean.y, ext.x, ext.y);
       p.records[3 * i + 1] = make_float4(conic.x, conic.y, conic.z, opacity);
       p.records[3 * i + 2] = make_float4(color.x, color.y, color.z, __int_as_float(i));

@@ -118,6 +118,7 @@ void fill_bin_params(BinParams& bp, const RasterLayout& L, char* ws, int N, int 
   bp.n_visible = &hdr->n_visible;
   bp.pair_count = &hdr->pair_count;
   bp.pair_capacity = capacity;
+  bp.tight = 0;
 }
 
 int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,

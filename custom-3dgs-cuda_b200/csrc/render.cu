@@ -228,8 +228,10 @@ extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const flo
                                  void* workspace, size_t workspace_bytes,
                                  long long pair_capacity, float* img, int* sorted_ids,
                                  int* tile_ranges, float* final_T, int* n_contrib, float* radii,
-                                 int* pair_count_host, void* m_ready_event, void* stream) {
+                                 int* pair_count_host, void* m_ready_event, unsigned flags,
+                                 void* stream) {
   GS_API_BEGIN();
+  GS_REQUIRE((flags & ~GS_RENDER_TIGHT_BINS) == 0u, "unknown render flag");
   GS_REQUIRE(N >= 0, "N must be non-negative");
   GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
   GS_REQUIRE((W + 15) / 16 < 65536 && (H + 15) / 16 < 65536, "image too large");
@@ -253,6 +255,7 @@ extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const flo
     PreprocessParams pp;
     fill_bin_params(pp.bin, L, ws, N, H, W, nullptr, nullptr, nullptr, nullptr, nullptr,
                     pair_capacity);
+    pp.bin.tight = (flags & GS_RENDER_TIGHT_BINS) ? 1 : 0;
     pp.mu = mu;
     pp.q = q;
     pp.s = s;

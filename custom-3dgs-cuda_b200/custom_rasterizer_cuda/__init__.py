@@ -163,23 +163,23 @@ def backwards_SH(colors_grad, mu, albedo, k_j, camera_position):
 
 # ---- rasterization -------------------------------------------------------------------------
 class _PairCapacity:
-    """Remembers the pair count M of earlier calls per (N, H, W) to size the next call's
-    pair buffers; a call whose M exceeds the guess is re-run with exactly M."""
+    """Remembers the pair count M of earlier calls per (N, H, W, binning mode) to size the next
+    call's pair buffers; a call whose M exceeds the guess is re-run with exactly M."""
 
     def __init__(self) -> None:
-        self._last: dict[tuple[int, int, int], int] = {}
+        self._last: dict[tuple[int, int, int, int], int] = {}
         self._lock = threading.Lock()
 
-    def guess(self, n: int, h: int, w: int) -> int:
+    def guess(self, n: int, h: int, w: int, mode: int = 0) -> int:
         with self._lock:
-            m = self._last.get((n, h, w))
+            m = self._last.get((n, h, w, mode))
         if m is None:
             return min(8 * n + 4096, (1 << 30) - 1)
         return min(m + m // 8 + 4096, (1 << 30) - 1)
 
-    def update(self, n: int, h: int, w: int, m: int) -> None:
+    def update(self, n: int, h: int, w: int, m: int, mode: int = 0) -> None:
         with self._lock:
-            self._last[(n, h, w)] = m
+            self._last[(n, h, w, mode)] = m
 
 
 _capacity = _PairCapacity()

@@ -44,7 +44,7 @@ SIGNATURES = {
     "gs_render_workspace_size": (c_size_t, [c_int, c_int, c_int, c_longlong]),
     "gs_render_forward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, c_float,
                                   c_float, c_float, c_float, P, c_size_t, c_longlong, P, P, P,
-                                  P, P, P, P, P, P]),
+                                  P, P, P, P, P, c_uint, P]),
     "gs_render_backward_workspace_size": (c_size_t, [c_int]),
     "gs_render_backward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, c_float,
                                    c_float, c_float, c_float, P, c_longlong, P, P, P, P, P,

@@ -31,8 +31,10 @@ class RenderState:
 
 
 def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy, height,
-                   width):
-    """(img[H,W,3], radii[N], RenderState). `opacity` is post-sigmoid, N or [N,1]."""
+                   width, tight_bins: bool = False):
+    """(img[H,W,3], radii[N], RenderState). `opacity` is post-sigmoid, N or [N,1].
+    tight_bins: bin splats only into tiles where they can pass the opacity test (same image
+    and gradients, shorter tile lists; the state's lists then differ from the reference's)."""
     N, H, W = int(mu.shape[0]), int(height), int(width)
     dev = mu.device
     T = _tiles(H, W)
@@ -43,7 +45,8 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
     n_contrib = torch.empty((H, W), **i32)
     tile_ranges = torch.empty((T, 2), **i32)
     radii = torch.empty((N,), **f32)
-    cap = _capacity.guess(N, H, W)
+    mode = 1 if tight_bins else 0
+    cap = _capacity.guess(N, H, W, mode)
     with torch.cuda.device(dev):
         stream = _stream(dev)
         m_host = torch.empty((1,), dtype=torch.int32, pin_memory=True)
@@ -57,10 +60,10 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
                 _ptr(R), _ptr(t), _ptr(cam_pos), float(fx), float(fy), float(cx), float(cy),
                 ws.data_ptr(), ws_bytes, cap, _ptr(img), sorted_ids.data_ptr(),
                 _ptr(tile_ranges), _ptr(final_T), _ptr(n_contrib), _ptr(radii),
-                m_host.data_ptr(), ev.handle, stream))
+                m_host.data_ptr(), ev.handle, mode, stream))
             ev.synchronize()
             M = int(m_host[0])
-            _capacity.update(N, H, W, M)
+            _capacity.update(N, H, W, M, mode)
             if M <= cap:
                 state = RenderState(ws, cap, sorted_ids, M, tile_ranges, final_T, n_contrib, H, W)
                 return img, radii, state

@@ -177,14 +177,16 @@ class Trainer:
     view's parameter gradients are added straight into the flat bucket, the densification
     statistics are updated inside the per-Gaussian backward kernel and the opacity gradient is
     taken through the sigmoid once per step. Consecutive views run on `view_streams`
-    alternating CUDA streams (1 = all on the current stream). mode "autograd" runs the same step through
+    alternating CUDA streams (1 = all on the current stream), and with `tight_bins` the splats
+    are binned only into tiles where they can pass the opacity test (same images and
+    gradients, shorter tile lists). mode "autograd" runs the same step through
     `gaussian_splatting.rasterizer.rasterize` (the drop-in RasterizeFunction) and
     loss.backward(), as the reference trainer does.
     """
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
                  fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct",
-                 view_streams: int = 3):
+                 view_streams: int = 3, tight_bins: bool = True):
         from gaussian_splatting.scene.gaussian import gaussian
 
         self.device = device
@@ -232,6 +234,7 @@ class Trainer:
         self.cam_positions = [(-torch.matmul(v["R"].T, v["T"])).reshape(3).contiguous()
                               for v in self.views]
         self.g_opacity = torch.zeros(scene.N, device=device, dtype=torch.float32)
+        self.tight_bins = tight_bins
         self._streams, self._accum_events = [], []
         if mode == "direct" and device.type == "cuda" and view_streams > 1:
             from custom_rasterizer_cuda import _lib
@@ -289,7 +292,7 @@ class Trainer:
                 with torch.cuda.stream(st):
                     img, _, rs = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
                                                 v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
-                                                v["width"])
+                                                v["width"], tight_bins=self.tight_bins)
                     target = targets.get(vi) if staged else targets[vi]
                     loss, gimg = l1_ssim_value_and_grad(img, target, LAMBDA_DSSIM)
                     if staged:

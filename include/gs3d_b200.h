@@ -159,6 +159,14 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
  * and statistic buffers waits for the first and the second is recorded after it, so that views
  * rendered concurrently on several streams can accumulate into the same buffers.
  */
+/* gs_render_forward flags. GS_RENDER_TIGHT_BINS: bin each splat only into the tiles of its
+ * reference rectangle that hold a pixel of its opacity-test extent box (the region where
+ * o exp(power) >= 1/255 can hold, inflated). The image, final_T and every gradient of
+ * gs_render_backward are unchanged, because the dropped pairs fail the opacity test at every
+ * pixel of their tile; M is smaller, so sorted_ids, tile_ranges and n_contrib (a list position)
+ * differ from the reference's. Without the flag all outputs match the reference's. */
+#define GS_RENDER_TIGHT_BINS 1u
+
 GS_API size_t gs_render_workspace_size(int N, int H, int W, long long pair_capacity);
 GS_API int gs_render_forward(int N, int H, int W, const float* mu, const float* q, const float* s,
                              const float* opacity, const float* albedo, const float* k_j,
@@ -167,7 +175,7 @@ GS_API int gs_render_forward(int N, int H, int W, const float* mu, const float* 
                              size_t workspace_bytes, long long pair_capacity, float* img,
                              int* sorted_ids, int* tile_ranges, float* final_T, int* n_contrib,
                              float* radii, int* pair_count_host, void* m_ready_event,
-                             void* stream);
+                             unsigned flags, void* stream);
 GS_API size_t gs_render_backward_workspace_size(int N);
 GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const float* mu,
                               const float* q, const float* s, const float* albedo,

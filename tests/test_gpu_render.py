@@ -86,3 +86,33 @@ def test_rasterize_function_attributes(cuda_device):
     img.sum().backward()
     assert RasterizeFunction.last_mean2d_grad.shape == (sc.N, 2)
     assert g.alpha.grad.shape == g.alpha.shape and torch.isfinite(g.alpha.grad).all()
+
+
+@pytest.mark.parametrize("case", list(scenes_small()), ids=lambda c: c[0])
+def test_tight_bins_keep_image_and_gradients(crc, cuda_device, case):
+    """GS_RENDER_TIGHT_BINS: image, transmittance and radii identical to the reference binning,
+    gradients within the atomic-order tolerance, and never more pairs."""
+    from custom_rasterizer_cuda.render import render_backward, render_forward
+
+    _, sc, view = case
+    dev = cuda_device
+    g = torch.Generator("cpu").manual_seed(5)
+    grad_img = torch.rand(view.height, view.width, 3, generator=g).to(dev)
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    R, t = view.R.to(dev).contiguous(), view.T.to(dev).contiguous()
+    cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+    op = torch.sigmoid(al).contiguous()
+    res = {}
+    for tight in (False, True):
+        img, radii, st = render_forward(mu, q, s, op, A, kj, R, t, cam, view.fx, view.fy,
+                                        view.cx, view.cy, view.height, view.width,
+                                        tight_bins=tight)
+        grads = render_backward(st, grad_img, mu, q, s, A, kj, R, t, cam, view.fx, view.fy,
+                                view.cx, view.cy)
+        res[tight] = (img, radii, st, grads)
+    (img0, radii0, st0, g0), (img1, radii1, st1, g1) = res[False], res[True]
+    assert torch.equal(img0, img1) and torch.equal(st0.final_T, st1.final_T)
+    assert torch.equal(radii0, radii1)
+    assert st1.pairs <= st0.pairs
+    for a, b, what in zip(g1, g0, ("mu", "q", "s", "opacity", "A", "kj", "mean2d")):
+        assert_grad_close(np32(a), np32(b), what + " (tight bins)")
