@@ -261,6 +261,78 @@ def per_view_breakdown(trainer, view: dict, reps: int = 5) -> dict:
             "fps": 1000.0 / statistics.median(fwd)}
 
 
+def render_table(dev, reps: int = 10) -> dict:
+    """Forward / backward ms and FPS through the drop-in `rasterize` / RasterizeFunction (the
+    reference's binning) on the other synthetic scenes: BASELINE configs 1-3 and the
+    reference's own bench scene (scripts/bench.py:30-63, the scene of its published numbers).
+    fwd/bwd ms are medians of CUDA-event-timed single calls; fps is back-to-back forwards (the
+    host's per-call work overlapping the previous frame), for config 3 over its 32 cameras."""
+    from gaussian_splatting.rasterizer.rasterize import rasterize
+    from gaussian_splatting.scene.gaussian import gaussian
+    from gs3d_b200 import scenes
+    from gs3d_b200.train_step import PARAM_NAMES
+
+    def gaussians_of(sc):
+        g = gaussian(sc.N)
+        for name, p in zip(PARAM_NAMES, sc.params()):
+            setattr(g, name, p.to(dev).contiguous().requires_grad_(True))
+        return g
+
+    def timed(fn):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        r = fn()
+        b.record()
+        return r, (a, b)
+
+    def fwd_bwd(g, view):
+        fw, bw = [], []
+        for i in range(reps + 2):
+            for name in PARAM_NAMES:
+                getattr(g, name).grad = None
+            img, ev_f = timed(lambda: rasterize(g, view))
+            grad = torch.ones_like(img)
+            _, ev_b = timed(lambda: img.backward(grad))
+            torch.cuda.synchronize()
+            if i >= 2:
+                fw.append(ev_f[0].elapsed_time(ev_f[1]))
+                bw.append(ev_b[0].elapsed_time(ev_b[1]))
+        with torch.no_grad():
+            for _ in range(2):
+                rasterize(g, view)
+            torch.cuda.synchronize()
+            _, ev = timed(lambda: [rasterize(g, view) for _ in range(reps)])
+            torch.cuda.synchronize()
+        return {"fwd_ms": statistics.median(fw), "bwd_ms": statistics.median(bw),
+                "fps": reps / (ev[0].elapsed_time(ev[1]) * 1e-3)}
+
+    out = {}
+    c1 = scenes.config1(0)
+    g1 = gaussians_of(c1)
+    out["config1_100k_1280x720"] = fwd_bwd(g1, c1.views[0].as_dict(dev))
+    out["config1_100k_1920x1080"] = fwd_bwd(g1, c1.views[1].as_dict(dev))
+    del g1
+    for w, h in ((1280, 720), (1920, 1080)):
+        rb = scenes.reference_bench_scene(width=w, height=h)
+        out[f"reference_bench_scene_100k_{w}x{h}"] = fwd_bwd(gaussians_of(rb),
+                                                             rb.views[0].as_dict(dev))
+    c2 = scenes.config2(0)
+    out["config2_1M_1920x1080"] = fwd_bwd(gaussians_of(c2), c2.views[0].as_dict(dev))
+    c3 = scenes.config3(0)
+    g3 = gaussians_of(c3)
+    views3 = [v.as_dict(dev) for v in c3.views]
+    with torch.no_grad():
+        for v in views3[:2]:
+            rasterize(g3, v)
+        torch.cuda.synchronize()
+        _, ev = timed(lambda: [rasterize(g3, v) for v in views3])
+        torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1])
+    out["config3_3M_3840x2160_32_cameras"] = {"fps": len(views3) / (ms * 1e-3),
+                                              "fwd_ms_per_frame": ms / len(views3)}
+    return out
+
+
 def view_pair_stats(trainer, views: list[dict]) -> dict:
     """Pairs M and replayed (pixel, Gaussian) pairs (sum of n_contrib) of each view, with the
     binning the trainer uses (with tight bins both count only the shorter lists' entries)."""
@@ -408,6 +480,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--gaussians", type=int, default=N_GAUSSIANS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-render-table", action="store_true",
+                    help="skip the per-scene forward/backward/FPS table (configs 1-3)")
     ap.add_argument("--view-streams", type=int, default=3,
                     help="CUDA streams the views of a step alternate over (1 = in order)")
     ap.add_argument("--view-only", action="store_true",
@@ -596,6 +670,8 @@ def run_ours(args, rank, world, local) -> int:
                 "d2h_bytes_per_step": 4 * world},
         "roofline": roofline_entry(stage_ms, stats, args.steps * len(mine), pk, args.gaussians),
     }
+    if world == 1 and not args.no_render_table:
+        line["render_table"] = render_table(dev)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(sc, sc.views[0], targets[0])
         line["cpu_baseline"].pop("seconds", None)
