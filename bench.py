@@ -261,7 +261,7 @@ def per_view_breakdown(trainer, view: dict, reps: int = 5) -> dict:
             "fps": 1000.0 / statistics.median(fwd)}
 
 
-def render_table(dev, reps: int = 10) -> dict:
+def render_table(dev, reps: int = 10, only=None) -> dict:
     """Forward / backward ms and FPS through the drop-in `rasterize` / RasterizeFunction (the
     reference's binning) on the other synthetic scenes: BASELINE configs 1-3 and the
     reference's own bench scene (scripts/bench.py:30-63, the scene of its published numbers).
@@ -301,23 +301,33 @@ def render_table(dev, reps: int = 10) -> dict:
             for _ in range(2):
                 rasterize(g, view)
             torch.cuda.synchronize()
-            _, ev = timed(lambda: [rasterize(g, view) for _ in range(reps)])
+            def frames():  # each image dropped as the next renders, as a render loop does
+                for _ in range(reps):
+                    rasterize(g, view)
+
+            _, ev = timed(frames)
             torch.cuda.synchronize()
         return {"fwd_ms": statistics.median(fw), "bwd_ms": statistics.median(bw),
                 "fps": reps / (ev[0].elapsed_time(ev[1]) * 1e-3)}
 
     out = {}
-    c1 = scenes.config1(0)
-    g1 = gaussians_of(c1)
-    out["config1_100k_1280x720"] = fwd_bwd(g1, c1.views[0].as_dict(dev))
-    out["config1_100k_1920x1080"] = fwd_bwd(g1, c1.views[1].as_dict(dev))
-    del g1
-    for w, h in ((1280, 720), (1920, 1080)):
-        rb = scenes.reference_bench_scene(width=w, height=h)
-        out[f"reference_bench_scene_100k_{w}x{h}"] = fwd_bwd(gaussians_of(rb),
-                                                             rb.views[0].as_dict(dev))
-    c2 = scenes.config2(0)
-    out["config2_1M_1920x1080"] = fwd_bwd(gaussians_of(c2), c2.views[0].as_dict(dev))
+    want = (lambda name: only is None or name in only)
+    if want("config1"):
+        c1 = scenes.config1(0)
+        g1 = gaussians_of(c1)
+        out["config1_100k_1280x720"] = fwd_bwd(g1, c1.views[0].as_dict(dev))
+        out["config1_100k_1920x1080"] = fwd_bwd(g1, c1.views[1].as_dict(dev))
+        del g1
+    if want("reference_bench"):
+        for w, h in ((1280, 720), (1920, 1080)):
+            rb = scenes.reference_bench_scene(width=w, height=h)
+            out[f"reference_bench_scene_100k_{w}x{h}"] = fwd_bwd(gaussians_of(rb),
+                                                                 rb.views[0].as_dict(dev))
+    if want("config2"):
+        c2 = scenes.config2(0)
+        out["config2_1M_1920x1080"] = fwd_bwd(gaussians_of(c2), c2.views[0].as_dict(dev))
+    if not want("config3"):
+        return out
     c3 = scenes.config3(0)
     g3 = gaussians_of(c3)
     views3 = [v.as_dict(dev) for v in c3.views]
@@ -325,7 +335,11 @@ def render_table(dev, reps: int = 10) -> dict:
         for v in views3[:2]:
             rasterize(g3, v)
         torch.cuda.synchronize()
-        _, ev = timed(lambda: [rasterize(g3, v) for v in views3])
+        def sweep():
+            for v in views3:
+                rasterize(g3, v)
+
+        _, ev = timed(sweep)
         torch.cuda.synchronize()
     ms = ev[0].elapsed_time(ev[1])
     out["config3_3M_3840x2160_32_cameras"] = {"fps": len(views3) / (ms * 1e-3),
@@ -487,9 +501,19 @@ def main() -> int:
     ap.add_argument("--view-only", action="store_true",
                     help="forward+backward of one config-2 view per step (single GPU); a small "
                          "fixed workload for profiler captures of single kernels")
+    ap.add_argument("--table-only", action="store_true",
+                    help="only the per-scene forward/backward/FPS table (single GPU)")
+    ap.add_argument("--table-scenes", default=None,
+                    help="comma list of config1,reference_bench,config2,config3 for the table")
     args = ap.parse_args()
     if args.view_only:
         return run_view(args)
+    if args.table_only:
+        torch.cuda.set_device(0)
+        only = set(args.table_scenes.split(",")) if args.table_scenes else None
+        emit({"mode": "render_table",
+              "render_table": render_table(torch.device("cuda", 0), only=only)})
+        return 0
     args.warmup_ref = min(args.warmup, 1)
     rank, world, local = init_dist(args.gpus)
     try:
