@@ -47,8 +47,7 @@ def _worker(rank: int, world: int, port: int, peer: bool, q) -> None:
     sys.path[:0] = [os.path.join(os.path.dirname(__file__), "..", "custom-3dgs-cuda_b200")]
     import torch.distributed as dist
 
-    if peer:
-        os.environ["GS3D_SHARD_PEER"] = "1"
+    os.environ["GS3D_SHARD_PEER"] = "1" if peer else "0"
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
