@@ -4,15 +4,16 @@
 // 4 rows apart, so warp w covers the 8 x (4 kPix) pixel block at ((w & 1) * 8, (w >> 1) * 4 kPix)
 // of the tile. Pixels of a thread share each splat-record load, the warp's cull test and, in
 // the backward, one warp reduction. The tile's depth-sorted splats are consumed in batches of
-// 256 blend records (48 bytes each) gathered with cp.async into a double-buffered
-// shared-memory ring: batch b + 1 is in flight while batch b is blended.
+// blend records (48 bytes each; 256 per batch forward, 128 backward) gathered with cp.async
+// into a double-buffered shared-memory ring: batch b + 1 is in flight while batch b is blended.
 #pragma once
 
 #include "gs_common.cuh"
 
 namespace gs {
 
-constexpr int kBlendBatch = 256;
+constexpr int kBlendBatch = 256;     // records per shared-memory batch, forward
+constexpr int kBlendBwdBatch = 128;  // backward: smaller rings leave room for 8 CTAs per SM
 constexpr int kBlendFwdPix = 2;  // pixels per thread of the forward blend
 constexpr int kBlendBwdPix = 2;  // pixels per thread of the backward blend
 
@@ -253,7 +254,9 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // moments St = sum(dL/dpower dx), Su = sum(dL/dpower dy), sum(dL/dpower dx dx), sum(dL/dpower dx dy),
 // sum(dL/dpower dy dy) and multiplied by the splat's conic at the flush; and the three
 // accumulated colours behind the splat enter dL/dalpha only through their dot product with
-// dL/dpixel, so one scalar D replaces them (D' = alpha (c . g) + (1 - alpha) D).
+// dL/dpixel, so one scalar D replaces them (D' = alpha (c . g) + (1 - alpha) D). A thread's
+// pixels share one column, so per pixel only sum(dL/dpower), sum(dL/dpower dy) and
+// sum(dL/dpower dy^2) are kept and the dx factors are applied once per splat.
 //
 // kFusedAccum selects the flush: false converts each tile's dL/dconic to dL/dSigma2 and adds
 // into the four reference-layout gradient arrays (9 scalar atomics, as the reference does);
@@ -262,10 +265,10 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 //   [2] = (dcol.b, -, -, -), and the conversion happens once per Gaussian later
 //   (dL/dSigma2 is linear in dL/dconic for a fixed conic, so the sums commute with it).
 template <bool kFusedAccum, int kPix>
-__global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(BlendBwdParams p) {
+__global__ void __launch_bounds__(kTilePixels / kPix, 10) blend_backward_kernel(BlendBwdParams p) {
   constexpr int kThreads = kTilePixels / kPix;
-  __shared__ float4 s_rec[2][3][kBlendBatch];
-  __shared__ float s_acc[kBlendBatch * kAccStride];
+  __shared__ float4 s_rec[2][3][kBlendBwdBatch];
+  __shared__ float s_acc[kBlendBwdBatch * kAccStride];
   __shared__ int s_max_last;
   const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
@@ -296,23 +299,23 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
     my_last = max(my_last, last[q]);
   }
   if (tid == 0) s_max_last = 0;
-  for (int k = tid; k < kBlendBatch * kAccStride; k += kThreads) s_acc[k] = 0.0f;
+  for (int k = tid; k < kBlendBwdBatch * kAccStride; k += kThreads) s_acc[k] = 0.0f;
   __syncthreads();
   const int warp_last = __reduce_max_sync(0xffffffffu, my_last);  // this warp's replay length
   if ((tid & 31) == 0 && warp_last > 0) atomicMax(&s_max_last, warp_last);
   __syncthreads();
   const int K_eff = s_max_last;  // list prefix that any pixel of this tile replays
-  const int nbatches = (K_eff + kBlendBatch - 1) / kBlendBatch;
+  const int nbatches = (K_eff + kBlendBwdBatch - 1) / kBlendBwdBatch;
 
   // batch b covers list indices [lo(b), hi(b)) walking from the back
-  auto batch_hi = [&](int b) { return K_eff - b * kBlendBatch; };
-  auto batch_lo = [&](int b) { return max(0, K_eff - (b + 1) * kBlendBatch); };
-  static_assert(kBlendBatch % kThreads == 0, "each thread issues whole records");
+  auto batch_hi = [&](int b) { return K_eff - b * kBlendBwdBatch; };
+  auto batch_lo = [&](int b) { return max(0, K_eff - (b + 1) * kBlendBwdBatch); };
+  static_assert(kBlendBwdBatch % kThreads == 0, "each thread issues whole records");
   auto issue = [&](int b) {
     const int lo = batch_lo(b), hi = batch_hi(b);
-    float4(*dst)[kBlendBatch] = s_rec[b & 1];
+    float4(*dst)[kBlendBwdBatch] = s_rec[b & 1];
 #pragma unroll
-    for (int r = 0; r < kBlendBatch / kThreads; ++r) {
+    for (int r = 0; r < kBlendBwdBatch / kThreads; ++r) {
       const int slot = tid + r * kThreads;
       const int j = lo + slot;
       if (j < hi) {
@@ -344,7 +347,7 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
     }
     __syncthreads();
     const int lo = batch_lo(b), hi = batch_hi(b);
-    const float4(*rec)[kBlendBatch] = s_rec[b & 1];
+    const float4(*rec)[kBlendBwdBatch] = s_rec[b & 1];
     // 32 list positions at a time from the back: lane l tests position top - 1 - l against
     // the warp's pixel block, the warp walks the hits back to front
     for (int top = min(hi, warp_last); top > lo; top -= 32) {
@@ -358,6 +361,9 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
         const int k = j - lo;  // slot in this batch
         const float4 r0 = rec[0][k];
         float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // the thread's pixels share one column (one dx): per pixel only sums over dL/dpower,
+        // dL/dpower dy and dL/dpower dy^2; dx enters once per splat below
+        float sp = 0.f, spy = 0.f, spyy = 0.f;
         bool active = false;
         const float4 r1 = rec[1][k];
         const float dx = fpx - r0.x;
@@ -382,22 +388,26 @@ __global__ void __launch_bounds__(kTilePixels / kPix) blend_backward_kernel(Blen
           v[6] += wgt * gg[q];
           v[7] += wgt * gb[q];
           const float cdotg = r2.x * gr[q] + r2.y * gg[q] + r2.z * gb[q];
-          const float dL_dalpha = (cdotg - D[q]) * T_before;
+          const float diff = cdotg - D[q];
+          const float dL_dalpha = diff * T_before;
           float dL_dpower = 0.0f;
           if (alpha_raw < 0.99f) {
             v[8] += G * dL_dalpha;
             dL_dpower = alpha * dL_dalpha;
           }
-          const float tx = dL_dpower * dx, ty = dL_dpower * dy;
-          v[0] += tx;
-          v[1] += ty;
-          v[2] += tx * dx;
-          v[3] += tx * dy;
-          v[4] += ty * dy;
-          D[q] = alpha * cdotg + one_minus * D[q];
+          const float ty = dL_dpower * dy;
+          sp += dL_dpower;
+          spy += ty;
+          spyy += ty * dy;
+          D[q] += alpha * diff;  // alpha cdotg + (1 - alpha) D
           T[q] = T_before;
         }
         if (__any_sync(0xffffffffu, active)) {
+          v[0] = sp * dx;   // sum dL/dpower dx
+          v[1] = spy;       // sum dL/dpower dy
+          v[2] = v[0] * dx; // sum dL/dpower dx^2
+          v[3] = spy * dx;  // sum dL/dpower dx dy
+          v[4] = spyy;      // sum dL/dpower dy^2
           float sum;
           int slot;
           warp_reduce9(v, &sum, &slot);
