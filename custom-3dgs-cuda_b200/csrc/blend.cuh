@@ -14,7 +14,7 @@ namespace gs {
 
 constexpr int kBlendBatch = 256;     // records per shared-memory batch, forward
 constexpr int kBlendBwdBatch = 128;  // backward: smaller rings leave room for 8 CTAs per SM
-constexpr int kBlendFwdPix = 2;  // pixels per thread of the forward blend
+constexpr int kBlendFwdPix = 1;  // pixels per thread of the forward blend
 constexpr int kBlendBwdPix = 2;  // pixels per thread of the backward blend
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
