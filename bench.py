@@ -371,8 +371,8 @@ def view_pair_stats(trainer, views: list[dict]) -> dict:
 # from one `ncu --set full --clock-control none` capture of a config-2 view (1M Gaussians of
 # the config-4 distribution at 1920x1080: `bench.py --view-only --steps 1 --warmup 1`).
 NCU_DRAM_BYTES = {
-    "preprocess": 259.9e6, "duplicate": 13.8e6, "blend_forward": 73.5e6,
-    "blend_backward": 142.7e6, "gaussian_backward": 490.0e6,
+    "preprocess": 259.1e6, "duplicate": 14.7e6, "blend_forward": 74.2e6,
+    "blend_backward": 142.4e6, "gaussian_backward": 489.7e6,
 }
 
 
