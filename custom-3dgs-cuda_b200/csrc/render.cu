@@ -57,6 +57,10 @@ __global__ void __launch_bounds__(kBinThreads) render_preprocess_kernel(Preproce
   const int tile = (int)blockIdx.x;
   const int i = tile * kBinThreads + tid;
 
+  // the warp's SH rows are copied into its stage while the projection runs
+  float* stage = s_stage + warp * 32 * kShRestFloats;
+  const bool rows_async =
+      warp_prefetch_rows<kShRestFloats>(pp.k_j, tile * kBinThreads + warp * 32, p.N, stage);
   Camera cam;
   load_camera(pp.R, pp.t, pp.fx, pp.fy, pp.cx, pp.cy, cam);
   Projected pr;
@@ -76,9 +80,13 @@ __global__ void __launch_bounds__(kBinThreads) render_preprocess_kernel(Preproce
       count = (unsigned)rect_count(r);
   }
   // SH colour only for splats that cover a tile; the warp stages its SH rows if any lane does
+  if (rows_async) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
   if (__ballot_sync(0xffffffffu, count > 0)) {
-    float* stage = s_stage + warp * 32 * kShRestFloats;
-    warp_load_rows<kShRestFloats>(pp.k_j, tile * kBinThreads + warp * 32, p.N, stage);
+    if (!rows_async)
+      warp_load_rows<kShRestFloats>(pp.k_j, tile * kBinThreads + warp * 32, p.N, stage);
     if (count > 0) {
       const float* kj = stage + lane * kShRestFloats;
       const float3 cp = make_float3(__ldg(pp.cam_pos), __ldg(pp.cam_pos + 1), __ldg(pp.cam_pos + 2));
@@ -130,6 +138,9 @@ __global__ void __launch_bounds__(256, 3) render_gaussian_backward_kernel(Gaussi
   if (row0 >= p.N) return;
   const int i = row0 + lane;
   const bool valid = i < p.N;
+  // the warp's SH rows are copied into its stage while the blend sums are read
+  float* stage = s_stage + warp * 32 * kShRestFloats;
+  const bool rows_async = warp_prefetch_rows<kShRestFloats>(p.k_j, row0, p.N, stage);
   float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, a2 = a0;
   if (valid) {
     a0 = p.accum[3 * i];
@@ -139,9 +150,13 @@ __global__ void __launch_bounds__(256, 3) render_gaussian_backward_kernel(Gaussi
   const bool touched = a0.x != 0.f || a0.y != 0.f || a0.z != 0.f || a0.w != 0.f ||
                        a1.x != 0.f || a1.y != 0.f || a1.z != 0.f || a1.w != 0.f || a2.x != 0.f;
   const bool acc = p.accumulate != 0;
-  float* stage = s_stage + warp * 32 * kShRestFloats;
   const bool warp_touched = __ballot_sync(0xffffffffu, touched) != 0u;
-  if (warp_touched) warp_load_rows<kShRestFloats>(p.k_j, row0, p.N, stage);
+  if (rows_async) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+  } else if (warp_touched) {
+    warp_load_rows<kShRestFloats>(p.k_j, row0, p.N, stage);
+  }
   float* row = stage + lane * kShRestFloats;
   if (valid && touched) {
     // dL/dconic -> dL/dSigma2 = -V G V with G's off-diagonal half of the packed sum
