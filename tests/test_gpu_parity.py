@@ -280,3 +280,55 @@ def test_full_size_properties_config2(crc, oracle, cuda_device):
     from custom_rasterizer_cuda import device_error_bits
 
     assert device_error_bits() == 0
+
+
+def test_speed_against_reference_kernels(crc, cuda_device):
+    """Config 2 (1M Gaussians, 1920x1080): the reference's own rasterize forward (count, CUB
+    scan, host sync, key generation, CUB 64-bit sort, ranges, blend) and blend backward kernels,
+    built from its sources by oracle/build_ref.py, against this library's `rasterize` /
+    `backwards_rasterization` on the same projected inputs. Both must agree; ours must not be
+    slower. Prints the CUDA-event medians (ms)."""
+    import statistics
+
+    from gs3d_b200 import scenes
+
+    ref = _ref_module()
+    sc = scenes.config2(0)
+    view = sc.views[0]
+    out = gpu_forward(crc, sc, view, cuda_device)
+    H, W = view.height, view.width
+    inputs = (sc.N, out["depths"], out["mean2d"], out["cov2d"], out["colors"], out["alpha"], H, W)
+    g = torch.rand(H, W, 3, device=cuda_device)
+
+    def timed(fn, reps=5):
+        ms = []
+        for k in range(reps + 2):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            res = fn()
+            b.record()
+            torch.cuda.synchronize()
+            if k >= 2:
+                ms.append(a.elapsed_time(b))
+        return res, statistics.median(ms)
+
+    fw = {}
+    for name, mod in (("reference", ref), ("ours", crc)):
+        res, ms = timed(lambda m=mod: m.rasterize(*inputs))
+        fw[name] = (res, ms)
+    r_img, r_ids, r_ranges, r_T, r_nc = fw["reference"][0]
+    assert torch.equal(r_ids, fw["ours"][0][1]) and torch.equal(r_img, fw["ours"][0][0])
+    bw = {}
+    for name, mod in (("reference", ref), ("ours", crc)):
+        args = (g, out["mean2d"], out["cov2d"], out["colors"], out["alpha"], r_ids, r_ranges,
+                r_T, r_nc, sc.N, H, W)
+        bw[name] = timed(lambda m=mod, a=args: m.backwards_rasterization(*a))
+    for a, b, what in zip(bw["ours"][0], bw["reference"][0], ("g_mean2d", "g_cov2d", "g_colors",
+                                                              "g_alpha")):
+        assert_grad_close(np32(a), np32(b), what)
+    f_ref, f_ours = fw["reference"][1], fw["ours"][1]
+    b_ref, b_ours = bw["reference"][1], bw["ours"][1]
+    print(f"\nconfig2 rasterize forward: reference {f_ref:.3f} ms, ours {f_ours:.3f} ms "
+          f"({f_ref / f_ours:.1f}x); backward: reference {b_ref:.3f} ms, ours {b_ours:.3f} ms "
+          f"({b_ref / b_ours:.1f}x); forward+backward {(f_ref + b_ref) / (f_ours + b_ours):.1f}x")
+    assert f_ours <= f_ref and b_ours <= b_ref
