@@ -263,7 +263,7 @@ def per_view_breakdown(trainer, view: dict, reps: int = 5) -> dict:
 
 def render_table(dev, reps: int = 10, only=None) -> dict:
     """Forward / backward ms and FPS through the drop-in `rasterize` / RasterizeFunction (the
-    reference's binning) on the other synthetic scenes: BASELINE configs 1-3 and the
+    reference's binning) on the other synthetic scenes: BASELINE configs 0-3 and the
     reference's own bench scene (scripts/bench.py:30-63, the scene of its published numbers).
     fwd/bwd ms are medians of CUDA-event-timed single calls; fps is back-to-back forwards (the
     host's per-call work overlapping the previous frame), for config 3 over its 32 cameras."""
@@ -312,6 +312,9 @@ def render_table(dev, reps: int = 10, only=None) -> dict:
 
     out = {}
     want = (lambda name: only is None or name in only)
+    if want("config0"):
+        c0 = scenes.config0(0)
+        out["config0_4096_128x128"] = fwd_bwd(gaussians_of(c0), c0.views[0].as_dict(dev))
     if want("config1"):
         c1 = scenes.config1(0)
         g1 = gaussians_of(c1)
@@ -504,7 +507,7 @@ def main() -> int:
     ap.add_argument("--table-only", action="store_true",
                     help="only the per-scene forward/backward/FPS table (single GPU)")
     ap.add_argument("--table-scenes", default=None,
-                    help="comma list of config1,reference_bench,config2,config3 for the table")
+                    help="comma list of config0,config1,reference_bench,config2,config3")
     args = ap.parse_args()
     if args.view_only:
         return run_view(args)
