@@ -73,17 +73,21 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
 
 def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, cam_pos, fx, fy,
                     cx, cy, want_mean2d_grad: bool = True, out=None, stats=None,
-                    accum_wait=None, accum_done=None):
+                    accum_wait=None, accum_done=None, accumulate=None):
     """Gradients (mu, q, s, opacity[N], albedo, k_j, mean2d or None). With `out` (a tuple of
     the first six buffers) the gradients are added into those buffers instead. `stats` =
     (norm_sum[N], count[N], norm_max[N], scale_x, scale_y) updates the densification
     statistics in the same pass. `accum_wait` / `accum_done` (`_lib.Event` or None) order the
-    kernel that writes `out` and `stats` after / before other streams' writes to them."""
+    kernel that writes `out` and `stats` after / before other streams' writes to them.
+    `accumulate=False` with `out` overwrites the six buffers instead (every element written);
+    the statistics are always added to."""
     N = int(mu.shape[0])
     dev = mu.device
     f32 = dict(device=dev, dtype=torch.float32)
-    accumulate = out is not None
+    if accumulate is None:
+        accumulate = out is not None
     if out is None:
+        accumulate = False
         out = (torch.empty((N, 3), **f32), torch.empty((N, 4), **f32), torch.empty((N, 3), **f32),
                torch.empty((N,), **f32), torch.empty((N, 3), **f32),
                torch.empty((N, 15, 3), **f32))

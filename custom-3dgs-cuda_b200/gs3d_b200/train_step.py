@@ -107,6 +107,12 @@ class FlatGrads:
         self.buffer.zero_()
         self.max_grad.zero_()
 
+    def zero_stats(self) -> None:
+        """Clears the densification statistics only (sums, counts, maxima)."""
+        self.grad_norm_sum.zero_()
+        self.grad_count.zero_()
+        self.max_grad.zero_()
+
     def rebind(self, params: list[torch.Tensor]) -> None:
         for p, v in zip(params, self.views):
             p.grad = v
@@ -266,9 +272,17 @@ class Trainer:
             targets.issue()
         g = self.gaussians
         fg = self.fg
-        fg.zero()
         fg.rebind(self.params)
-        self.g_opacity.zero_()
+        views = self.plan.views()
+        if views:
+            # the first view's backward overwrites every parameter gradient (and g_opacity), so
+            # only the statistics and the opacity-logit slice (written through the sigmoid
+            # below) need clearing
+            fg.zero_stats()
+            g.alpha.grad.zero_()
+        else:
+            fg.zero()
+            self.g_opacity.zero_()
         with torch.no_grad():
             mu, q, s, A, kj = g.mu.detach(), g.q.detach(), g.s.detach(), g.A.detach(), g.k_j.detach()
             opacity = torch.sigmoid(g.alpha.detach()).reshape(-1)
@@ -282,7 +296,7 @@ class Trainer:
                 if st is not main:
                     st.wait_stream(main)
             losses, prev_done = [], None
-            for k, vi in enumerate(self.plan.views()):
+            for k, vi in enumerate(views):
                 v = self.views[vi]
                 cam = self.cam_positions[vi]
                 if before_view is not None:
@@ -301,7 +315,7 @@ class Trainer:
                                     v["fy"], v["cx"], v["cy"], want_mean2d_grad=False, out=out,
                                     stats=(fg.grad_norm_sum, fg.grad_count, fg.max_grad,
                                            v["width"] / 2.0, v["height"] / 2.0),
-                                    accum_wait=prev_done, accum_done=done)
+                                    accum_wait=prev_done, accum_done=done, accumulate=k > 0)
                 prev_done = done
                 if st is not main:
                     loss.record_stream(main)
