@@ -2,8 +2,9 @@
 // on [H, W, 3] images, SSIM with an 11x11 Gaussian window (sigma 1.5, zero padding,
 // C1 = 0.01^2, C2 = 0.03^2), averaged over pixels and channels.
 //
-// Forward (one kernel + a one-block reduction): each CTA stages a 32x16 output tile plus a
-// 5-pixel halo of x and y in shared memory (one plane per channel), blurs the five moments
+// Forward (one kernel + a one-block reduction): each CTA takes a 32x32 output tile and, one
+// channel at a time, stages that channel's x and y with a 5-pixel halo in shared memory, blurs
+// the five moments
 // (x, y, x^2, y^2, xy) of the three channels separably (11 horizontal taps into shared memory,
 // then 11 vertical taps; each thread produces a run of 8 outputs from an 18-value window held
 // in registers, so a tap costs an FMA and no shared-memory load), forms the SSIM map and, per
@@ -13,36 +14,40 @@
 //   A  = dS/dmu_x - 2 mu_x B - mu_y Cm
 // so that d(sum_p S_p)/dx_q = (G*A)(q) + 2 x_q (G*B)(q) + y_q (G*Cm)(q). Per-block partial sums
 // of S and |x - y| (in double) are reduced in a fixed order, so the loss is deterministic.
-// Backward: the same tiling blurs A, B, Cm and combines them with x, y and sign(x - y).
+// Backward: the same tiling, a channel at a time, blurs A, B, Cm and combines them with x,
+// y and sign(x - y). One channel's planes (41 KB / 37 KB of shared memory) leave room for 5-6
+// CTAs per SM.
 #include "capi_internal.h"
 #include "gs_common.cuh"
 
 namespace gs {
 
-constexpr int kSsimTW = 32, kSsimTH = 16, kSsimR = 5, kSsimTaps = 11;
+constexpr int kSsimTW = 32, kSsimTH = 32, kSsimR = 5, kSsimTaps = 11;
 constexpr int kSsimInW = kSsimTW + 2 * kSsimR;  // 42
-constexpr int kSsimInH = kSsimTH + 2 * kSsimR;  // 26
+constexpr int kSsimInH = kSsimTH + 2 * kSsimR;  // 42
 constexpr int kSsimRun = 8;                     // outputs per thread and blur pass
 constexpr int kSsimWin = kSsimRun + kSsimTaps - 1;  // 18 inputs per run
-constexpr int kSsimThreads = 192;
+constexpr int kSsimThreads = 128;
 constexpr int kSsimWarps = kSsimThreads / 32;
 constexpr float kSsimC1 = 0.01f * 0.01f, kSsimC2 = 0.03f * 0.03f;
 static_assert(kSsimTW % kSsimRun == 0 && kSsimTH % kSsimRun == 0, "runs tile the output");
-static_assert(3 * kSsimTW * (kSsimTH / kSsimRun) == kSsimThreads, "one vertical run per thread");
+static_assert(kSsimTW * (kSsimTH / kSsimRun) == kSsimThreads,
+              "one vertical run per thread and channel");
 
 __constant__ float c_gauss[kSsimTaps];
 
-// Planar per-channel staging; h holds the horizontal blurs of the 5 moments of 3 channels.
+// One channel at a time: its input planes and the horizontal blurs of its 5 moments.
 struct SsimForwardSmem {
-  float x[3][kSsimInH][kSsimInW];
-  float y[3][kSsimInH][kSsimInW];
-  float h[15][kSsimInH][kSsimTW];
+  float x[kSsimInH][kSsimInW];
+  float y[kSsimInH][kSsimInW];
+  float h[5][kSsimInH][kSsimTW];
   double part[2][kSsimWarps];
 };
 
+// One channel at a time: its A, B, Cm planes and their horizontal blurs.
 struct SsimBackwardSmem {
-  float m[9][kSsimInH][kSsimInW];  // A, B, Cm x 3 channels
-  float h[9][kSsimInH][kSsimTW];
+  float m[3][kSsimInH][kSsimInW];
+  float h[3][kSsimInH][kSsimTW];
 };
 
 // out[o] = sum_t g[t] in[o + t] for a run of kSsimRun outputs (registers only).
@@ -74,122 +79,120 @@ __device__ __forceinline__ void store_run(float* dst, const float (&v)[kSsimRun]
 }
 
 // Derivative maps are planar: maps[(3 * kind + channel) * H * W + pixel], kind A, B, Cm.
-__global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
+__global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
     int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
     float* __restrict__ maps, double* __restrict__ partials) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SsimForwardSmem& s = *reinterpret_cast<SsimForwardSmem*>(smem_raw);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bx = blockIdx.x * kSsimTW, by = blockIdx.y * kSsimTH;
   const int x0 = bx - kSsimR, y0 = by - kSsimR;
-  double l1_sum = 0.0;
-  // coalesced loads of the interleaved rows, de-interleaved into planes; the L1 term is
-  // summed here over the tile's own (non-halo) pixels
-  // one warp per halo row (126 interleaved floats, lanes along the row), all of a warp's rows
-  // loaded before any is stored
-  {
-    constexpr int kRowF = kSsimInW * 3;
-    constexpr int kRowsPerWarp = (kSsimInH + kSsimWarps - 1) / kSsimWarps;
-    constexpr int kChunks = (kRowF + 31) / 32;
-    const int warp = tid >> 5, lane = tid & 31;
-    float a[kRowsPerWarp][kChunks], b[kRowsPerWarp][kChunks];
+  const size_t HW = (size_t)H * W;
+  // this thread's vertical run: column col, output rows [rb * 8, rb * 8 + 8)
+  const int rb = tid / kSsimTW, col = tid % kSsimTW;
+  const int gx = bx + col;
+  double ssim_sum = 0.0, l1_sum = 0.0;
+#pragma unroll 1
+  for (int c = 0; c < 3; ++c) {
+    // channel c of the halo rows: one warp per row, lanes along it, 6 rows in flight per warp
+    {
+      constexpr int kRowsPerWarp = (kSsimInH + kSsimWarps - 1) / kSsimWarps;
+      constexpr int kBatch = 6;
+#pragma unroll 1
+      for (int r0 = 0; r0 < kRowsPerWarp; r0 += kBatch) {
+        float a[kBatch][2], b[kBatch][2];
 #pragma unroll
-    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-      const int py = warp + rr * kSsimWarps, gy = y0 + py;
-      const bool row_ok = py < kSsimInH && gy >= 0 && gy < H;
+        for (int rr = 0; rr < kBatch; ++rr) {
+          const int py = warp + (r0 + rr) * kSsimWarps, gy = y0 + py;
+          const bool row_ok = r0 + rr < kRowsPerWarp && py < kSsimInH && gy >= 0 && gy < H;
 #pragma unroll
-      for (int u = 0; u < kChunks; ++u) {
-        const int f = lane + 32 * u, gf = 3 * x0 + f;
-        a[rr][u] = b[rr][u] = 0.f;
-        if (row_ok && f < kRowF && gf >= 0 && gf < 3 * W) {
-          const size_t o = (size_t)gy * W * 3 + gf;
-          a[rr][u] = __ldg(img + o);
-          b[rr][u] = __ldg(ref + o);
+          for (int u = 0; u < 2; ++u) {
+            const int px = lane + 32 * u, gxx = x0 + px;
+            a[rr][u] = b[rr][u] = 0.f;
+            if (row_ok && px < kSsimInW && gxx >= 0 && gxx < W) {
+              const size_t o = ((size_t)gy * W + gxx) * 3 + c;
+              a[rr][u] = __ldg(img + o);
+              b[rr][u] = __ldg(ref + o);
+            }
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < kBatch; ++rr) {
+          const int py = warp + (r0 + rr) * kSsimWarps;
+          if (r0 + rr >= kRowsPerWarp || py >= kSsimInH) break;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int px = lane + 32 * u;
+            if (px < kSsimInW) {
+              s.x[py][px] = a[rr][u];
+              s.y[py][px] = b[rr][u];
+            }
+          }
         }
       }
     }
+    __syncthreads();
+    // horizontal: runs of 8 outputs of the 5 moments
+    for (int it = tid; it < kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
+      const int r = it / (kSsimTW / kSsimRun), cb = it - r * (kSsimTW / kSsimRun);
+      float xa[kSsimWin], ya[kSsimWin], w[kSsimWin], out[kSsimRun];
+      load_row_window(&s.x[r][cb * kSsimRun], xa);
+      load_row_window(&s.y[r][cb * kSsimRun], ya);
+      blur_run(xa, out);
+      store_run(&s.h[0][r][cb * kSsimRun], out);
+      blur_run(ya, out);
+      store_run(&s.h[1][r][cb * kSsimRun], out);
 #pragma unroll
-    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-      const int py = warp + rr * kSsimWarps;
-      if (py >= kSsimInH) break;
+      for (int k = 0; k < kSsimWin; ++k) w[k] = xa[k] * xa[k];
+      blur_run(w, out);
+      store_run(&s.h[2][r][cb * kSsimRun], out);
 #pragma unroll
-      for (int u = 0; u < kChunks; ++u) {
-        const int f = lane + 32 * u;
-        if (f >= kRowF) break;
-        const int px = f / 3, c = f - 3 * px;
-        if (px >= kSsimR && px < kSsimR + kSsimTW && py >= kSsimR && py < kSsimR + kSsimTH)
-          l1_sum += (double)fabsf(a[rr][u] - b[rr][u]);  // zero outside the image
-        s.x[c][py][px] = a[rr][u];
-        s.y[c][py][px] = b[rr][u];
+      for (int k = 0; k < kSsimWin; ++k) w[k] = ya[k] * ya[k];
+      blur_run(w, out);
+      store_run(&s.h[3][r][cb * kSsimRun], out);
+#pragma unroll
+      for (int k = 0; k < kSsimWin; ++k) w[k] = xa[k] * ya[k];
+      blur_run(w, out);
+      store_run(&s.h[4][r][cb * kSsimRun], out);
+    }
+    __syncthreads();
+    // vertical run, SSIM and its derivative maps
+    {
+      float m[5][kSsimRun];
+#pragma unroll
+      for (int q = 0; q < 5; ++q) {
+        float v[kSsimWin];
+#pragma unroll
+        for (int k = 0; k < kSsimWin; ++k) v[k] = s.h[q][rb * kSsimRun + k][col];
+        blur_run(v, m[q]);
       }
+      float run_ssim = 0.f, run_l1 = 0.f;  // at most 8 terms each; summed in double below
+#pragma unroll
+      for (int o = 0; o < kSsimRun; ++o) {
+        const int r = rb * kSsimRun + o, gy = by + r;
+        if (gx >= W || gy >= H) continue;
+        const float mx = m[0][o], my = m[1][o];
+        const float vx = m[2][o] - mx * mx, vy = m[3][o] - my * my, cxy = m[4][o] - mx * my;
+        const float n1 = 2.f * mx * my + kSsimC1, n2 = 2.f * cxy + kSsimC2;
+        const float d1 = mx * mx + my * my + kSsimC1, d2 = vx + vy + kSsimC2;
+        // one reciprocal: 1/den, 1/d1 = d2/den, 1/d2 = d1/den
+        const float rden = 1.0f / (d1 * d2);
+        const float S = n1 * n2 * rden;
+        const float B = -S * (d1 * rden);
+        const float Cm = 2.f * n1 * rden;
+        const float dmx = 2.f * my * n2 * rden - 2.f * mx * S * (d2 * rden);
+        const float A = dmx - 2.f * mx * B - my * Cm;
+        const size_t pix = (size_t)gy * W + gx;
+        maps[(0 + c) * HW + pix] = A;
+        maps[(3 + c) * HW + pix] = B;
+        maps[(6 + c) * HW + pix] = Cm;
+        run_ssim += S;
+        run_l1 += fabsf(s.x[r + kSsimR][col + kSsimR] - s.y[r + kSsimR][col + kSsimR]);
+      }
+      ssim_sum += (double)run_ssim;
+      l1_sum += (double)run_l1;
     }
-  }
-  __syncthreads();
-  // horizontal: one run of 8 outputs of the 5 moments of one channel per item
-  for (int it = tid; it < 3 * kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
-    const int c = it / (kSsimInH * (kSsimTW / kSsimRun));
-    const int rem = it - c * (kSsimInH * (kSsimTW / kSsimRun));
-    const int r = rem / (kSsimTW / kSsimRun), cb = rem - r * (kSsimTW / kSsimRun);
-    float xa[kSsimWin], ya[kSsimWin], w[kSsimWin], out[kSsimRun];
-    load_row_window(&s.x[c][r][cb * kSsimRun], xa);
-    load_row_window(&s.y[c][r][cb * kSsimRun], ya);
-    blur_run(xa, out);
-    store_run(&s.h[c * 5 + 0][r][cb * kSsimRun], out);
-    blur_run(ya, out);
-    store_run(&s.h[c * 5 + 1][r][cb * kSsimRun], out);
-#pragma unroll
-    for (int k = 0; k < kSsimWin; ++k) w[k] = xa[k] * xa[k];
-    blur_run(w, out);
-    store_run(&s.h[c * 5 + 2][r][cb * kSsimRun], out);
-#pragma unroll
-    for (int k = 0; k < kSsimWin; ++k) w[k] = ya[k] * ya[k];
-    blur_run(w, out);
-    store_run(&s.h[c * 5 + 3][r][cb * kSsimRun], out);
-#pragma unroll
-    for (int k = 0; k < kSsimWin; ++k) w[k] = xa[k] * ya[k];
-    blur_run(w, out);
-    store_run(&s.h[c * 5 + 4][r][cb * kSsimRun], out);
-  }
-  __syncthreads();
-  // vertical: each thread one column run of 8 pixels of one channel
-  double ssim_sum = 0.0;
-  {
-    const int c = tid / (kSsimTW * (kSsimTH / kSsimRun));
-    const int rem = tid - c * (kSsimTW * (kSsimTH / kSsimRun));
-    const int rb = rem / kSsimTW, col = rem - rb * kSsimTW;
-    float m[5][kSsimRun];
-#pragma unroll
-    for (int q = 0; q < 5; ++q) {
-      float v[kSsimWin];
-#pragma unroll
-      for (int k = 0; k < kSsimWin; ++k) v[k] = s.h[c * 5 + q][rb * kSsimRun + k][col];
-      blur_run(v, m[q]);
-    }
-    const int gx = bx + col;
-    const size_t HW = (size_t)H * W;
-    float run_sum = 0.f;  // at most 8 terms in [-1, 1]; summed in double across runs
-#pragma unroll
-    for (int o = 0; o < kSsimRun; ++o) {
-      const int gy = by + rb * kSsimRun + o;
-      if (gx >= W || gy >= H) continue;
-      const float mx = m[0][o], my = m[1][o];
-      const float vx = m[2][o] - mx * mx, vy = m[3][o] - my * my, cxy = m[4][o] - mx * my;
-      const float n1 = 2.f * mx * my + kSsimC1, n2 = 2.f * cxy + kSsimC2;
-      const float d1 = mx * mx + my * my + kSsimC1, d2 = vx + vy + kSsimC2;
-      // one reciprocal: 1/den, 1/d1 = d2/den, 1/d2 = d1/den
-      const float r = 1.0f / (d1 * d2);
-      const float S = n1 * n2 * r;
-      const float B = -S * (d1 * r);
-      const float Cm = 2.f * n1 * r;
-      const float dmx = 2.f * my * n2 * r - 2.f * mx * S * (d2 * r);
-      const float A = dmx - 2.f * mx * B - my * Cm;
-      const size_t pix = (size_t)gy * W + gx;
-      maps[(0 + c) * HW + pix] = A;
-      maps[(3 + c) * HW + pix] = B;
-      maps[(6 + c) * HW + pix] = Cm;
-      run_sum += S;
-    }
-    ssim_sum += (double)run_sum;
+    __syncthreads();  // the next channel overwrites the planes
   }
   // block reduction in a fixed order
 #pragma unroll
@@ -197,9 +200,9 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_forward_kernel(
     ssim_sum += __shfl_xor_sync(0xffffffffu, ssim_sum, o);
     l1_sum += __shfl_xor_sync(0xffffffffu, l1_sum, o);
   }
-  if ((tid & 31) == 0) {
-    s.part[0][tid >> 5] = ssim_sum;
-    s.part[1][tid >> 5] = l1_sum;
+  if (lane == 0) {
+    s.part[0][warp] = ssim_sum;
+    s.part[1][warp] = l1_sum;
   }
   __syncthreads();
   if (tid == 0) {
@@ -241,85 +244,86 @@ __global__ void __launch_bounds__(256) ssim_finalize_kernel(const double* __rest
   }
 }
 
-__global__ void __launch_bounds__(kSsimThreads) ssim_backward_kernel(
+__global__ void __launch_bounds__(kSsimThreads, 6) ssim_backward_kernel(
     int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
     const float* __restrict__ maps, const float* __restrict__ grad_loss, float lambda,
     float inv_n, float* __restrict__ grad_img) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SsimBackwardSmem& s = *reinterpret_cast<SsimBackwardSmem*>(smem_raw);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bx = blockIdx.x * kSsimTW, by = blockIdx.y * kSsimTH;
   const int x0 = bx - kSsimR, y0 = by - kSsimR;
   const size_t HW = (size_t)H * W;
-  {
-    // one warp per halo row of one map plane (lanes along the row), 8 rows in flight per warp
-    constexpr int kRows = 9 * kSsimInH;
-    constexpr int kRowsPerWarp = (kRows + kSsimWarps - 1) / kSsimWarps;
-    constexpr int kBatch = 8;
-    const int warp = tid >> 5, lane = tid & 31;
+  const float g = __ldg(grad_loss);
+  const float w_l1 = g * (1.0f - lambda) * inv_n, w_ssim = -g * lambda * inv_n;
+  const int rb = tid / kSsimTW, col = tid % kSsimTW;
+  const int gx = bx + col;
 #pragma unroll 1
-    for (int r0 = 0; r0 < kRowsPerWarp; r0 += kBatch) {
-      float v[kBatch][2];
+  for (int c = 0; c < 3; ++c) {
+    // planes A_c, B_c, Cm_c: one warp per halo row, 8 rows in flight per warp
+    {
+      constexpr int kRows = 3 * kSsimInH;
+      constexpr int kRowsPerWarp = (kRows + kSsimWarps - 1) / kSsimWarps;
+      constexpr int kBatch = 8;
+#pragma unroll 1
+      for (int r0 = 0; r0 < kRowsPerWarp; r0 += kBatch) {
+        float v[kBatch][2];
 #pragma unroll
-      for (int rr = 0; rr < kBatch; ++rr) {
-        const int row = warp + (r0 + rr) * kSsimWarps;
-        const int q = row / kSsimInH, py = row - q * kSsimInH, gy = y0 + py;
-        const bool row_ok = r0 + rr < kRowsPerWarp && row < kRows && gy >= 0 && gy < H;
+        for (int rr = 0; rr < kBatch; ++rr) {
+          const int row = warp + (r0 + rr) * kSsimWarps;
+          const int kind = row / kSsimInH, py = row - kind * kSsimInH, gy = y0 + py;
+          const bool row_ok = r0 + rr < kRowsPerWarp && row < kRows && gy >= 0 && gy < H;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int px = lane + 32 * u, gx = x0 + px;
-          v[rr][u] = (row_ok && px < kSsimInW && gx >= 0 && gx < W)
-                         ? __ldg(maps + q * HW + (size_t)gy * W + gx)
-                         : 0.f;
+          for (int u = 0; u < 2; ++u) {
+            const int px = lane + 32 * u, gxx = x0 + px;
+            v[rr][u] = (row_ok && px < kSsimInW && gxx >= 0 && gxx < W)
+                           ? __ldg(maps + (3 * kind + c) * HW + (size_t)gy * W + gxx)
+                           : 0.f;
+          }
         }
-      }
 #pragma unroll
-      for (int rr = 0; rr < kBatch; ++rr) {
-        const int row = warp + (r0 + rr) * kSsimWarps;
-        if (r0 + rr >= kRowsPerWarp || row >= kRows) break;
-        const int q = row / kSsimInH, py = row - q * kSsimInH;
+        for (int rr = 0; rr < kBatch; ++rr) {
+          const int row = warp + (r0 + rr) * kSsimWarps;
+          if (r0 + rr >= kRowsPerWarp || row >= kRows) break;
+          const int kind = row / kSsimInH, py = row - kind * kSsimInH;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int px = lane + 32 * u;
-          if (px < kSsimInW) s.m[q][py][px] = v[rr][u];
+          for (int u = 0; u < 2; ++u) {
+            const int px = lane + 32 * u;
+            if (px < kSsimInW) s.m[kind][py][px] = v[rr][u];
+          }
         }
       }
     }
-  }
-  __syncthreads();
-  for (int it = tid; it < 9 * kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
-    const int q = it / (kSsimInH * (kSsimTW / kSsimRun));
-    const int rem = it - q * (kSsimInH * (kSsimTW / kSsimRun));
-    const int r = rem / (kSsimTW / kSsimRun), cb = rem - r * (kSsimTW / kSsimRun);
-    float w[kSsimWin], out[kSsimRun];
-    load_row_window(&s.m[q][r][cb * kSsimRun], w);
-    blur_run(w, out);
-    store_run(&s.h[q][r][cb * kSsimRun], out);
-  }
-  __syncthreads();
-  const float g = __ldg(grad_loss);
-  const float w_l1 = g * (1.0f - lambda) * inv_n, w_ssim = -g * lambda * inv_n;
-  const int c = tid / (kSsimTW * (kSsimTH / kSsimRun));
-  const int rem = tid - c * (kSsimTW * (kSsimTH / kSsimRun));
-  const int rb = rem / kSsimTW, col = rem - rb * kSsimTW;
-  float bl[3][kSsimRun];
+    __syncthreads();
+    for (int it = tid; it < 3 * kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
+      const int kind = it / (kSsimInH * (kSsimTW / kSsimRun));
+      const int rem = it - kind * (kSsimInH * (kSsimTW / kSsimRun));
+      const int r = rem / (kSsimTW / kSsimRun), cb = rem - r * (kSsimTW / kSsimRun);
+      float w[kSsimWin], out[kSsimRun];
+      load_row_window(&s.m[kind][r][cb * kSsimRun], w);
+      blur_run(w, out);
+      store_run(&s.h[kind][r][cb * kSsimRun], out);
+    }
+    __syncthreads();
+    float bl[3][kSsimRun];
 #pragma unroll
-  for (int kind = 0; kind < 3; ++kind) {
-    float v[kSsimWin];
+    for (int kind = 0; kind < 3; ++kind) {
+      float v[kSsimWin];
 #pragma unroll
-    for (int k = 0; k < kSsimWin; ++k) v[k] = s.h[3 * kind + c][rb * kSsimRun + k][col];
-    blur_run(v, bl[kind]);
-  }
-  const int gx = bx + col;
+      for (int k = 0; k < kSsimWin; ++k) v[k] = s.h[kind][rb * kSsimRun + k][col];
+      blur_run(v, bl[kind]);
+    }
 #pragma unroll
-  for (int o = 0; o < kSsimRun; ++o) {
-    const int gy = by + rb * kSsimRun + o;
-    if (gx >= W || gy >= H) continue;
-    const size_t p = ((size_t)gy * W + gx) * 3 + c;
-    const float xv = __ldg(img + p), yv = __ldg(ref + p);
-    const float d = xv - yv;
-    const float sgn = d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
-    grad_img[p] = w_l1 * sgn + w_ssim * (bl[0][o] + 2.f * xv * bl[1][o] + yv * bl[2][o]);
+    for (int o = 0; o < kSsimRun; ++o) {
+      const int gy = by + rb * kSsimRun + o;
+      if (gx >= W || gy >= H) continue;
+      const size_t p = ((size_t)gy * W + gx) * 3 + c;
+      const float xv = __ldg(img + p), yv = __ldg(ref + p);
+      const float d = xv - yv;
+      const float sgn = d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
+      grad_img[p] = w_l1 * sgn + w_ssim * (bl[0][o] + 2.f * xv * bl[1][o] + yv * bl[2][o]);
+    }
+    __syncthreads();  // the next channel overwrites the planes
   }
 }
 
