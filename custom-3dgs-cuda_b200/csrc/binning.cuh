@@ -199,17 +199,18 @@ struct DupParams {
 
 // Exclusive scan of the tile counts in depth order and duplication of each Gaussian into
 // one (tile id, Gaussian index) pair per covered tile, row-major over its rectangle
-// (the order of csrc/forward/rasterize.cu:124-135). A block's pairs are contiguous, so
-// the block writes them cooperatively: pair p belongs to the Gaussian whose exclusive
-// offset is the last one <= p.
+// (the order of csrc/forward/rasterize.cu:124-135). A warp's 32 Gaussians own a contiguous run
+// of pairs, which the warp writes 32 at a time: lanes where a Gaussian's pairs start in the
+// current window record their lane in a per-warp table and the window's start positions are
+// OR-reduced into one mask; pair lane q takes the Gaussian of the highest start at or below q
+// (or the one carried from the previous window) and fetches its rectangle by shuffle.
 static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p) {
   __shared__ unsigned s_tile, s_prefix;
   __shared__ unsigned s_scan[33];
-  __shared__ unsigned s_off[kBinThreads];
-  __shared__ uint2 s_rect[kBinThreads];
-  __shared__ unsigned s_gid[kBinThreads];
+  __shared__ unsigned s_owner[kBinThreads / 32][32];
   __shared__ unsigned s_hist[4][256];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr unsigned kFull = 0xffffffffu;
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int nv = *p.n_visible;
   const int num_tiles = (nv + kBinThreads - 1) / kBinThreads;
@@ -238,9 +239,6 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
       s_prefix = prefix;
     }
   }
-  s_off[tid] = excl;
-  s_rect[tid] = pr;
-  s_gid[tid] = gid;
   __syncthreads();
   const unsigned base = s_prefix;
   const unsigned M = (unsigned)*p.pair_count;
@@ -248,24 +246,48 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
     if (tid == 0) raise_device_error(kErrBadIndex);
     return;
   }
-  for (unsigned q = tid; q < tile_pairs; q += kBinThreads) {
-    // last k with s_off[k] <= q
-    int lo = 0, hi = kBinThreads - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (s_off[mid] <= q) lo = mid; else hi = mid - 1;
-    }
-    const TileRect r = unpack_rect(s_rect[lo]);
-    const unsigned w = (unsigned)(r.x1 - r.x0);
-    const unsigned lp = q - s_off[lo];
-    const unsigned row = lp / w, col = lp - row * w;
-    const unsigned tile_id = (unsigned)(r.y0 + row) * (unsigned)p.tiles_x + (unsigned)r.x0 + col;
-    p.tile_keys[base + q] = tile_id;
-    p.tile_vals[base + q] = s_gid[lo];
+  // this warp's run of pairs: [w_first, w_first + w_total) of the block's
+  const unsigned w_first = __shfl_sync(kFull, excl, 0);
+  const unsigned w_total = __shfl_sync(kFull, excl + count, 31) - w_first;
+  const unsigned my_o = excl - w_first;
+  const TileRect mine = unpack_rect(pr);
+  const unsigned my_w = count > 0 ? (unsigned)(mine.x1 - mine.x0) : 1u;
+  const float my_inv_w = 1.0f / (float)my_w;
+  unsigned* table = s_owner[warp];
+  const unsigned le = lane == 31 ? kFull : ((2u << lane) - 1u);  // lanes 0..lane
+  int carried = 0;
+  for (unsigned wb = 0; wb < w_total; wb += 32) {
+    const bool starts_here = count > 0 && my_o >= wb && my_o < wb + 32;
+    if (starts_here) table[my_o - wb] = (unsigned)lane;
+    const unsigned starts = __reduce_or_sync(kFull, starts_here ? 1u << (my_o - wb) : 0u);
+    __syncwarp();
+    const unsigned m = starts & le;
+    const int owner = m ? (int)table[31 - __clz(m)] : carried;
+    const unsigned o_own = __shfl_sync(kFull, my_o, owner);
+    const unsigned rx = __shfl_sync(kFull, pr.x, owner), ry = __shfl_sync(kFull, pr.y, owner);
+    const unsigned g_own = __shfl_sync(kFull, gid, owner);
+    const float inv_w = __shfl_sync(kFull, my_inv_w, owner);
+    const unsigned q = wb + (unsigned)lane;
+    if (q < w_total) {
+      const TileRect r = unpack_rect(make_uint2(rx, ry));
+      const unsigned w = (unsigned)(r.x1 - r.x0);
+      const unsigned lp = q - o_own;
+      // row = lp / w from the float reciprocal, then made exact
+      unsigned row = (unsigned)(((float)lp + 0.5f) * inv_w);
+      if (row * w > lp) --row;
+      if ((row + 1) * w <= lp) ++row;
+      const unsigned col = lp - row * w;
+      const unsigned tile_id =
+          (unsigned)(r.y0 + (int)row) * (unsigned)p.tiles_x + (unsigned)r.x0 + col;
+      p.tile_keys[base + w_first + q] = tile_id;
+      p.tile_vals[base + w_first + q] = g_own;
 #pragma unroll
-    for (int pass = 0; pass < 4; ++pass)  // constant indices keep the parameters in registers
-      if (pass < p.n_tile_passes)
-        atomicAdd(&s_hist[pass][(tile_id >> p.tile_shift[pass]) & p.tile_mask[pass]], 1u);
+      for (int pass = 0; pass < 4; ++pass)  // constant indices keep the parameters in registers
+        if (pass < p.n_tile_passes)
+          atomicAdd(&s_hist[pass][(tile_id >> p.tile_shift[pass]) & p.tile_mask[pass]], 1u);
+    }
+    carried = __shfl_sync(kFull, owner, 31);
+    __syncwarp();  // the next window rewrites the table
   }
   __syncthreads();
   for (int k = tid; k < p.n_tile_passes * 256; k += kBinThreads) {

@@ -54,20 +54,37 @@ def _reduce_worker(rank: int, world: int, port: int, batch: int, q) -> None:
         dist.destroy_process_group()
 
 
+def _run_ranks(target, world, extra, attempts=2):
+    """Spawns `world` ranks of `target(rank, world, port, *extra, queue)` and collects one
+    queue item per rank; a second attempt with a fresh port covers a port another process took
+    between _free_port() and the rendezvous."""
+    import queue as queue_mod
+
+    ctx = mp.get_context("spawn")
+    for attempt in range(attempts):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=target, args=(r, world, port, *extra, q))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        try:
+            results = [q.get(timeout=120) for _ in range(world)]
+        except queue_mod.Empty:
+            results = None
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+        if results is not None and all(p.exitcode == 0 for p in procs):
+            return results
+    raise AssertionError("ranks did not complete")
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_view_sharding_and_reductions(world):
     batch = 8
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, batch, q))
-             for r in range(world)]
-    for p in procs:
-        p.start()
-    results = [q.get(timeout=120) for _ in range(world)]
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    results = _run_ranks(_reduce_worker, world, (batch,))
     # every view rendered exactly once across ranks
     all_views = sorted(v for _, views, *_ in results for v in views)
     assert all_views == list(range(batch))
