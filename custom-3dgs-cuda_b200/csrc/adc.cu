@@ -1,0 +1,334 @@
+// Adaptive density control on the device: the clone / split / prune / opacity-reset step of
+// the reference trainer (gaussian_splatting/utils/adc.py:330-392), which the reference runs
+// as Python over torch ops with host syncs. Two calls:
+//
+// gs_adc_plan classifies every Gaussian (one thread each) with the reference's rules:
+//   g = nan_to_num(grad_accum / max(denom, 1)), m = max_k exp(s_k), o = sigmoid(alpha);
+//   clone if densify and g >= threshold and m <= percent_dense * extent,
+//   split if densify and g >= threshold and m >  percent_dense * extent;
+//   a Gaussian, its clone and its two split children are pruned when o < min_opacity or
+//   their largest scale exceeds 0.1 * extent or (max_screen_size given) their screen radius
+//   does (the radius of a new Gaussian is 0; a child's scales are exp(log(exp(s) / 1.6))).
+// It writes a decision byte per Gaussian and, per block of 256, the number of kept
+// originals, kept clones, split Gaussians, kept children and clones; one CTA then scans the block
+// counts into block offsets and totals, which reach the host through a pinned copy.
+//
+// gs_adc_apply writes the result in the reference's order, [kept originals][kept clones]
+// [kept first children][kept second children], each in index order: parameters copied (a
+// child's mean is R(q) (z * exp(s)) + mu with the caller's unit normals z, its log-scales
+// log(exp(s) / 1.6)), Adam moments copied for originals and zero for new Gaussians, and
+// with the opacity reset alpha = min(alpha, logit(0.01)) and zero opacity moments.
+#include <algorithm>
+#include <cmath>
+
+#include "capi_internal.h"
+#include "gs_common.cuh"
+
+namespace gs {
+
+constexpr int kAdcThreads = 256;
+constexpr int kAdcScanThreads = 1024;
+constexpr int kAdcGroups = 6;
+constexpr int kAdcCats = 5;  // kept originals, kept clones, split, kept children, clones
+__constant__ int c_adc_dims[kAdcGroups] = {3, 4, 3, 1, 3, 45};  // mu, q, s, alpha, A, k_j
+
+enum : unsigned char {
+  kAdcClone = 1, kAdcSplit = 2, kAdcKeepOrig = 4, kAdcKeepClone = 8, kAdcKeepChild = 16,
+};
+
+struct AdcRules {
+  float grad_threshold, pd_line, big_line, min_opacity, max_screen;  // max_screen < 0: none
+  int densify, prune;
+};
+
+struct AdcLayout {  // workspace: decisions, per-block counts and offsets, totals
+  size_t flags, counts, offsets, totals, total;
+  int blocks;
+};
+
+static AdcLayout adc_layout(int N) {
+  AdcLayout L;
+  L.blocks = (N + kAdcThreads - 1) / kAdcThreads;
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    const size_t at = off;
+    off += (b + 255) / 256 * 256;
+    return at;
+  };
+  L.flags = take((size_t)std::max(N, 1));
+  L.counts = take((size_t)std::max(L.blocks, 1) * kAdcCats * sizeof(unsigned));
+  L.offsets = take((size_t)std::max(L.blocks, 1) * kAdcCats * sizeof(unsigned));
+  L.totals = take(kAdcCats * sizeof(long long));
+  L.total = off;
+  return L;
+}
+
+__device__ __forceinline__ float adc_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__global__ void __launch_bounds__(kAdcThreads) adc_classify_kernel(
+    int N, const float* __restrict__ s, const float* __restrict__ alpha,
+    const float* __restrict__ grad_accum, const float* __restrict__ denom,
+    const float* __restrict__ max_radii, AdcRules r, unsigned char* __restrict__ flags,
+    unsigned* __restrict__ block_counts) {
+  __shared__ unsigned s_cnt[kAdcCats];
+  const int i = blockIdx.x * kAdcThreads + threadIdx.x;
+  if (threadIdx.x < kAdcCats) s_cnt[threadIdx.x] = 0u;
+  __syncthreads();
+  unsigned char f = 0;
+  if (i < N) {
+    float g = grad_accum[i] / fmaxf(denom[i], 1.0f);
+    if (g != g) g = 0.0f;  // nan_to_num(nan=0); +-inf map to the finite extremes
+    if (isinf(g)) g = g > 0.0f ? 3.402823466e38f : -3.402823466e38f;
+    const float e0 = expf(s[3 * i]), e1 = expf(s[3 * i + 1]), e2 = expf(s[3 * i + 2]);
+    const float m = fmaxf(fmaxf(e0, e1), e2);
+    const bool grad_ok = r.densify && g >= r.grad_threshold;
+    const bool clone = grad_ok && m <= r.pd_line;
+    const bool split = grad_ok && m > r.pd_line;
+    const float o = adc_sigmoid(alpha[i]);
+    const float c0 = expf(logf(e0 / 1.6f)), c1 = expf(logf(e1 / 1.6f)), c2 = expf(logf(e2 / 1.6f));
+    const float mc = fmaxf(fmaxf(c0, c1), c2);
+    const bool low = o < r.min_opacity;
+    const bool prune_orig =
+        r.prune && (low || m > r.big_line || (r.max_screen >= 0.0f && max_radii[i] > r.max_screen));
+    // a new Gaussian's screen radius is 0, so only its opacity and scales can prune it
+    const bool prune_new = r.prune && (low || m > r.big_line);
+    const bool prune_child = r.prune && (low || mc > r.big_line);
+    f = (clone ? kAdcClone : 0) | (split ? kAdcSplit : 0) |
+        (!split && !prune_orig ? kAdcKeepOrig : 0) | (clone && !prune_new ? kAdcKeepClone : 0) |
+        (split && !prune_child ? kAdcKeepChild : 0);
+    flags[i] = f;
+  }
+  const unsigned full = 0xffffffffu;
+  const unsigned a = __popc(__ballot_sync(full, f & kAdcKeepOrig));
+  const unsigned b = __popc(__ballot_sync(full, f & kAdcKeepClone));
+  const unsigned c = __popc(__ballot_sync(full, f & kAdcSplit));
+  const unsigned d = __popc(__ballot_sync(full, f & kAdcKeepChild));
+  const unsigned e = __popc(__ballot_sync(full, f & kAdcClone));
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(&s_cnt[0], a);
+    atomicAdd(&s_cnt[1], b);
+    atomicAdd(&s_cnt[2], c);
+    atomicAdd(&s_cnt[3], d);
+    atomicAdd(&s_cnt[4], e);
+  }
+  __syncthreads();
+  if (threadIdx.x < kAdcCats)
+    block_counts[kAdcCats * blockIdx.x + threadIdx.x] = s_cnt[threadIdx.x];
+}
+
+// One CTA: exclusive scan of the per-block counts of each category; totals last.
+__global__ void __launch_bounds__(kAdcScanThreads) adc_scan_kernel(
+    int blocks, const unsigned* __restrict__ counts, unsigned* __restrict__ offsets,
+    long long* __restrict__ totals) {
+  __shared__ unsigned s_scan[33];
+  for (int cat = 0; cat < kAdcCats; ++cat) {
+    unsigned carry = 0;
+    for (int b0 = 0; b0 < blocks; b0 += kAdcScanThreads) {
+      const int b = b0 + threadIdx.x;
+      const unsigned v = b < blocks ? counts[kAdcCats * b + cat] : 0u;
+      unsigned chunk;
+      const unsigned ex = block_exclusive_scan(v, s_scan, &chunk);
+      if (b < blocks) offsets[kAdcCats * b + cat] = carry + ex;
+      carry += chunk;
+    }
+    if (threadIdx.x == 0) totals[cat] = (long long)carry;
+  }
+}
+
+struct AdcApply {
+  int N;
+  const unsigned char* flags;
+  const unsigned* offsets;
+  long long n_orig, n_clone, n_child;  // kept originals, kept clones, kept children per copy
+  long long n_split;                   // split Gaussians (rows of z per copy)
+  const float* in[kAdcGroups];
+  const float* m_in[kAdcGroups];
+  const float* v_in[kAdcGroups];
+  float* out[kAdcGroups];
+  float* m_out[kAdcGroups];
+  float* v_out[kAdcGroups];
+  const float* z;
+  int reset_opacity;
+  float opacity_cap;  // logit(0.01)
+};
+
+__device__ __forceinline__ unsigned block_rank(bool pred, unsigned* s_warp, unsigned* total) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned ballot = __ballot_sync(full, pred);
+  if (lane == 0) s_warp[warp] = __popc(ballot);
+  __syncthreads();
+  unsigned before = 0, all = 0;
+  for (int w = 0; w < kAdcThreads / 32; ++w) {
+    const unsigned c = s_warp[w];
+    if (w < warp) before += c;
+    all += c;
+  }
+  __syncthreads();
+  *total = all;
+  return before + __popc(ballot & ((1u << lane) - 1u));
+}
+
+__device__ __forceinline__ void copy_row(const AdcApply& a, int k, int src, long long dst,
+                                         bool moments_from_src, bool reset) {
+  const int d = c_adc_dims[k];
+  const float* in = a.in[k] + (size_t)src * d;
+  float* out = a.out[k] + (size_t)dst * d;
+  for (int j = 0; j < d; ++j) {
+    float v = in[j];
+    if (k == 3 && reset) v = fminf(v, a.opacity_cap);
+    out[j] = v;
+  }
+  const bool zero = !moments_from_src || (k == 3 && reset);
+  if (a.m_out[k]) {
+    float* mo = a.m_out[k] + (size_t)dst * d;
+    const float* mi = a.m_in[k] + (size_t)src * d;
+    for (int j = 0; j < d; ++j) mo[j] = zero ? 0.0f : mi[j];
+  }
+  if (a.v_out[k]) {
+    float* vo = a.v_out[k] + (size_t)dst * d;
+    const float* vi = a.v_in[k] + (size_t)src * d;
+    for (int j = 0; j < d; ++j) vo[j] = zero ? 0.0f : vi[j];
+  }
+}
+
+__global__ void __launch_bounds__(kAdcThreads) adc_apply_kernel(AdcApply a) {
+  __shared__ unsigned s_warp[kAdcThreads / 32];
+  const int i = blockIdx.x * kAdcThreads + threadIdx.x;
+  const unsigned char f = i < a.N ? a.flags[i] : 0;
+  const unsigned* off = a.offsets + kAdcCats * blockIdx.x;
+  unsigned tot;
+  const unsigned r_orig = block_rank(f & kAdcKeepOrig, s_warp, &tot);
+  const unsigned r_clone = block_rank(f & kAdcKeepClone, s_warp, &tot);
+  const unsigned r_split = block_rank(f & kAdcSplit, s_warp, &tot);
+  const unsigned r_child = block_rank(f & kAdcKeepChild, s_warp, &tot);
+  if (i >= a.N) return;
+  const bool reset = a.reset_opacity != 0;
+  if (f & kAdcKeepOrig) {
+    const long long dst = (long long)off[0] + r_orig;
+    for (int k = 0; k < kAdcGroups; ++k) copy_row(a, k, i, dst, true, reset);
+  }
+  if (f & kAdcKeepClone) {
+    const long long dst = a.n_orig + (long long)off[1] + r_clone;
+    for (int k = 0; k < kAdcGroups; ++k) copy_row(a, k, i, dst, false, reset);
+  }
+  if (f & kAdcKeepChild) {
+    const long long row = (long long)off[2] + r_split;  // this Gaussian's rank among splits
+    const long long ci = (long long)off[3] + r_child;
+    const float* mu = a.in[0] + 3 * (size_t)i;
+    const float* q = a.in[1] + 4 * (size_t)i;
+    const float* s = a.in[2] + 3 * (size_t)i;
+    const float nq = sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
+    const float inv = 1.0f / fmaxf(nq, 1e-12f);
+    const float w = q[0] * inv, x = q[1] * inv, y = q[2] * inv, z = q[3] * inv;
+    const float R[3][3] = {
+        {1.0f - 2.0f * (y * y + z * z), 2.0f * (x * y - w * z), 2.0f * (x * z + w * y)},
+        {2.0f * (x * y + w * z), 1.0f - 2.0f * (x * x + z * z), 2.0f * (y * z - w * x)},
+        {2.0f * (x * z - w * y), 2.0f * (y * z + w * x), 1.0f - 2.0f * (x * x + y * y)}};
+    const float e[3] = {expf(s[0]), expf(s[1]), expf(s[2])};
+    for (int copy = 0; copy < 2; ++copy) {
+      const long long dst = a.n_orig + a.n_clone + copy * a.n_child + ci;
+      const float* zr = a.z + 3 * (size_t)(copy * a.n_split + row);
+      const float smp[3] = {0.0f + zr[0] * e[0], 0.0f + zr[1] * e[1], 0.0f + zr[2] * e[2]};
+      for (int k = 0; k < kAdcGroups; ++k) copy_row(a, k, i, dst, false, reset);
+      float* mo = a.out[0] + 3 * (size_t)dst;
+      float* so = a.out[2] + 3 * (size_t)dst;
+      for (int c = 0; c < 3; ++c) {
+        mo[c] = (R[c][0] * smp[0] + R[c][1] * smp[1] + R[c][2] * smp[2]) + mu[c];
+        so[c] = logf(e[c] / 1.6f);
+      }
+    }
+  }
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" size_t gs_adc_workspace_size(int N) {
+  if (N < 0) return 0;
+  return adc_layout(N).total;
+}
+
+extern "C" int gs_adc_plan(int N, const float* s, const float* alpha, const float* grad_accum,
+                           const float* denom, const float* max_radii, float grad_threshold,
+                           float percent_dense_extent, float big_extent, float min_opacity,
+                           float max_screen_size, int densify, int prune, void* workspace,
+                           size_t workspace_bytes, long long* totals_host, void* done_event,
+                           void* stream) {
+  GS_API_BEGIN();
+  GS_REQUIRE(N >= 0, "N must be non-negative");
+  const AdcLayout L = adc_layout(N);
+  GS_REQUIRE(workspace && workspace_bytes >= L.total, "workspace too small");
+  GS_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0u,
+             "workspace must be 256-byte aligned");
+  GS_REQUIRE(N == 0 || (s && alpha && grad_accum && denom && max_radii), "null input pointer");
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  long long* totals = reinterpret_cast<long long*>(ws + L.totals);
+  if (N == 0) {
+    GS_CUDA(cudaMemsetAsync(totals, 0, kAdcCats * sizeof(long long), st));
+  } else {
+    AdcRules r{grad_threshold, percent_dense_extent, big_extent, min_opacity, max_screen_size,
+               densify ? 1 : 0, prune ? 1 : 0};
+    adc_classify_kernel<<<L.blocks, kAdcThreads, 0, st>>>(
+        N, s, alpha, grad_accum, denom, max_radii, r,
+        reinterpret_cast<unsigned char*>(ws + L.flags), reinterpret_cast<unsigned*>(ws + L.counts));
+    GS_CHECK_LAUNCH();
+    adc_scan_kernel<<<1, kAdcScanThreads, 0, st>>>(
+        L.blocks, reinterpret_cast<const unsigned*>(ws + L.counts),
+        reinterpret_cast<unsigned*>(ws + L.offsets), totals);
+    GS_CHECK_LAUNCH();
+  }
+  if (totals_host)
+    GS_CUDA(cudaMemcpyAsync(totals_host, totals, kAdcCats * sizeof(long long),
+                            cudaMemcpyDeviceToHost, st));
+  if (done_event) GS_CUDA(cudaEventRecord((cudaEvent_t)done_event, st));
+  return GS_OK;
+  GS_API_END();
+}
+
+extern "C" int gs_adc_apply(int N, const void* workspace, size_t workspace_bytes,
+                            const long long* totals, const float* const* params,
+                            const float* const* exp_avg, const float* const* exp_avg_sq,
+                            const float* z, int reset_opacity, float* const* out_params,
+                            float* const* out_exp_avg, float* const* out_exp_avg_sq,
+                            void* stream) {
+  GS_API_BEGIN();
+  GS_REQUIRE(N >= 0, "N must be non-negative");
+  const AdcLayout L = adc_layout(N);
+  GS_REQUIRE(workspace && workspace_bytes >= L.total, "workspace too small");
+  GS_REQUIRE(totals && params && out_params, "null pointer");
+  GS_REQUIRE(totals[0] >= 0 && totals[1] >= 0 && totals[2] >= 0 && totals[3] >= 0 &&
+                 totals[0] <= N && totals[1] <= N && totals[3] <= totals[2] && totals[2] <= N,
+             "totals do not come from gs_adc_plan for this N");
+  GS_REQUIRE(totals[2] == 0 || z, "null split samples");
+  if (N == 0) return GS_OK;
+  AdcApply a{};
+  a.N = N;
+  const char* ws = static_cast<const char*>(workspace);
+  a.flags = reinterpret_cast<const unsigned char*>(ws + L.flags);
+  a.offsets = reinterpret_cast<const unsigned*>(ws + L.offsets);
+  a.n_orig = totals[0];
+  a.n_clone = totals[1];
+  a.n_split = totals[2];
+  a.n_child = totals[3];
+  for (int k = 0; k < kAdcGroups; ++k) {
+    GS_REQUIRE(params[k] && out_params[k], "null parameter pointer");
+    a.in[k] = params[k];
+    a.out[k] = out_params[k];
+    const bool has_m = exp_avg && exp_avg[k] && out_exp_avg && out_exp_avg[k];
+    const bool has_v = exp_avg_sq && exp_avg_sq[k] && out_exp_avg_sq && out_exp_avg_sq[k];
+    a.m_in[k] = has_m ? exp_avg[k] : nullptr;
+    a.m_out[k] = has_m ? out_exp_avg[k] : nullptr;
+    a.v_in[k] = has_v ? exp_avg_sq[k] : nullptr;
+    a.v_out[k] = has_v ? out_exp_avg_sq[k] : nullptr;
+  }
+  a.z = z;
+  a.reset_opacity = reset_opacity ? 1 : 0;
+  a.opacity_cap = (float)std::log(0.01 / (1.0 - 0.01));
+  adc_apply_kernel<<<L.blocks, kAdcThreads, 0, (cudaStream_t)stream>>>(a);
+  GS_CHECK_LAUNCH();
+  return GS_OK;
+  GS_API_END();
+}

@@ -56,6 +56,10 @@ SIGNATURES = {
     "gs_adam_step": (c_int, [c_int, P, P, P, P, P, P, c_double, c_double, c_double, c_longlong, P]),
     "gs_sharded_adam_step": (c_int, [P, P, P, c_int, P, P, c_double, c_double, c_double,
                                      c_longlong, c_float, P]),
+    "gs_adc_workspace_size": (c_size_t, [c_int]),
+    "gs_adc_plan": (c_int, [c_int, P, P, P, P, P, c_float, c_float, c_float, c_float, c_float,
+                            c_int, c_int, P, c_size_t, P, P, P]),
+    "gs_adc_apply": (c_int, [c_int, P, c_size_t, P, P, P, P, P, c_int, P, P, P, P]),
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),

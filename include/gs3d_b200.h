@@ -264,6 +264,39 @@ GS_API int gs_sharded_adam_step(const gs_shard_buffers* buffers, float* exp_avg,
                                 long long step, float grad_scale, void* stream);
 
 /*
+ * Adaptive density control (the reference trainer's clone / split / prune / opacity reset,
+ * gaussian_splatting/utils/adc.py:330-392, which the reference runs as torch ops with host
+ * syncs) in two calls; no counterpart in the reference's extension.
+ * gs_adc_plan classifies the N Gaussians from log-scales s[N,3], opacity logits alpha[N],
+ * the densification statistics (grad_accum[N], denom[N], max_radii[N]) and the thresholds
+ * (percent_dense_extent = percent_dense * extent and big_extent = 0.1 * extent, both rounded
+ * to float as torch compares them; max_screen_size < 0: no screen-size rule; densify: the
+ * reference's allow_densify and N < max_gaussians; prune: allow_densify). It writes five totals
+ * to totals_host (pinned): kept originals, kept clones, split Gaussians, kept children per copy,
+ * clones before pruning; and records done_event after the copy.
+ * gs_adc_apply (same N and workspace, the first four totals on the host) writes the new set of
+ * totals[0] + totals[1] + 2 * totals[3] Gaussians in the reference's order (kept originals,
+ * kept clones, kept first children, kept second children; each in index order): params and
+ * out_params are host arrays of the six device pointers mu[.,3], q[.,4], s[.,3], alpha[.,1],
+ * A[.,3], k_j[.,15,3]; the optional Adam moments in the same layout are copied for originals
+ * and zeroed for new Gaussians; z holds 2 * totals[2] unit normals [.,3] (rows [0, n) for the
+ * first child of each split Gaussian in index order, [n, 2n) for the second); reset_opacity
+ * caps alpha at logit(0.01) and zeroes its moments.
+ */
+GS_API size_t gs_adc_workspace_size(int N);
+GS_API int gs_adc_plan(int N, const float* s, const float* alpha, const float* grad_accum,
+                       const float* denom, const float* max_radii, float grad_threshold,
+                       float percent_dense_extent, float big_extent, float min_opacity,
+                       float max_screen_size, int densify, int prune, void* workspace,
+                       size_t workspace_bytes, long long* totals_host, void* done_event,
+                       void* stream);
+GS_API int gs_adc_apply(int N, const void* workspace, size_t workspace_bytes,
+                        const long long* totals, const float* const* params,
+                        const float* const* exp_avg, const float* const* exp_avg_sq,
+                        const float* z, int reset_opacity, float* const* out_params,
+                        float* const* out_exp_avg, float* const* out_exp_avg_sq, void* stream);
+
+/*
  * CUDA event helpers for m_ready_event (cudaEvent_t values passed as void*): create an event
  * with timing disabled, block the calling thread until it completes, destroy it.
  */
