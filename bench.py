@@ -683,6 +683,9 @@ def run_ours(args, rank, world, local) -> int:
         "stage_ms_per_view": stage_ms,
         "view_streams": len(trainer._streams) or 1,
         "tight_bins": trainer.tight_bins,
+        "blend_variant": ("throughput: 2 / 4 pixels per thread forward / backward"
+                          if trainer.concurrent_views else
+                          "latency: 1 / 2 pixels per thread forward / backward"),
         "update_ms_per_step": update_ms,
         "update_phases_ms_rank0": update_phases,
         "update": ("fused reduce-scatter + sharded Adam + all-gather (multicast)"

@@ -4,7 +4,7 @@
 // 4 rows apart, so warp w covers the 8 x (4 kPix) pixel block at ((w & 1) * 8, (w >> 1) * 4 kPix)
 // of the tile. Pixels of a thread share each splat-record load, the warp's cull test and, in
 // the backward, one warp reduction. The tile's depth-sorted splats are consumed in batches of
-// blend records (48 bytes each; 256 per batch forward, 128 backward) gathered with cp.async
+// blend records (48 bytes each; 256 per batch forward, 128 or 64 backward) gathered with cp.async
 // into a double-buffered shared-memory ring: batch b + 1 is in flight while batch b is blended.
 #pragma once
 
@@ -12,10 +12,28 @@
 
 namespace gs {
 
-constexpr int kBlendBatch = 256;     // records per shared-memory batch, forward
-constexpr int kBlendBwdBatch = 128;  // backward: smaller rings leave room for 8 CTAs per SM
-constexpr int kBlendFwdPix = 1;  // pixels per thread of the forward blend
-constexpr int kBlendBwdPix = 2;  // pixels per thread of the backward blend
+constexpr int kBlendBatch = 256;  // records per shared-memory batch, forward
+
+// Pixels per thread. A thread's pixels share each record load, the warp's cull test and (in
+// the backward) one warp reduction per splat, so more pixels per thread means fewer
+// instructions per pixel, but fewer threads per tile and a longer kernel when it runs alone.
+// The latency variants serve one view at a time; the throughput variants are for views that
+// overlap on several streams (GS_RENDER_CONCURRENT), where the SMs are shared with other
+// kernels and the instruction count sets the pace (config-4 step on one B200: 565 -> 584
+// views/s, although each blend kernel alone is 3% / 26% slower).
+constexpr int kBlendFwdPix = 1;            // forward, one view at a time
+constexpr int kBlendFwdPixThroughput = 2;  // forward, overlapped views
+constexpr int kBlendBwdPix = 2;            // backward, one view at a time
+constexpr int kBlendBwdPixThroughput = 4;  // backward, overlapped views
+
+// Backward shared-memory batch (records) and resident CTAs per SM: 128 records and 10 CTAs of
+// 128 threads (43 registers) at two pixels per thread; 64 records and 16 CTAs of 64 threads
+// (56 registers) at four.
+template <int kPix>
+struct BlendBwdShape {
+  static constexpr int kBatch = kPix >= 4 ? 64 : 128;
+  static constexpr int kMinBlocks = kPix >= 4 ? 16 : 10;
+};
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -265,8 +283,10 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 //   [2] = (dcol.b, -, -, -), and the conversion happens once per Gaussian later
 //   (dL/dSigma2 is linear in dL/dconic for a fixed conic, so the sums commute with it).
 template <bool kFusedAccum, int kPix>
-__global__ void __launch_bounds__(kTilePixels / kPix, 10) blend_backward_kernel(BlendBwdParams p) {
+__global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinBlocks)
+    blend_backward_kernel(BlendBwdParams p) {
   constexpr int kThreads = kTilePixels / kPix;
+  constexpr int kBlendBwdBatch = BlendBwdShape<kPix>::kBatch;
   __shared__ float4 s_rec[2][3][kBlendBwdBatch];
   __shared__ float s_acc[kBlendBwdBatch * kAccStride];
   __shared__ int s_max_last;

@@ -123,7 +123,8 @@ void fill_bin_params(BinParams& bp, const RasterLayout& L, char* ws, int N, int 
 
 int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
                           long long capacity, float* img, int* sorted_ids, int* tile_ranges,
-                          float* final_T, int* n_contrib, cudaStream_t stream) {
+                          float* final_T, int* n_contrib, bool throughput,
+                          cudaStream_t stream) {
   RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
   float4* records = reinterpret_cast<float4*>(ws + L.records);
   unsigned* dk[2] = {reinterpret_cast<unsigned*>(ws + L.depth_keys[0]),
@@ -224,8 +225,13 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
   fp.img = img;
   fp.final_T = final_T;
   fp.n_contrib = n_contrib;
-  blend_forward_kernel<kBlendFwdPix>
-      <<<(unsigned)L.T, kTilePixels / kBlendFwdPix, 0, stream>>>(fp);
+  if (throughput) {
+    blend_forward_kernel<kBlendFwdPixThroughput>
+        <<<(unsigned)L.T, kTilePixels / kBlendFwdPixThroughput, 0, stream>>>(fp);
+  } else {
+    blend_forward_kernel<kBlendFwdPix>
+        <<<(unsigned)L.T, kTilePixels / kBlendFwdPix, 0, stream>>>(fp);
+  }
   GS_CHECK_LAUNCH();
   mark_stage(6, stream);
   return GS_OK;
@@ -254,7 +260,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
                             cudaMemcpyDeviceToHost, stream));
   if (m_ready) GS_CUDA(cudaEventRecord(m_ready, stream));
   return launch_sort_and_blend(L, N, H, W, ws, capacity, img, sorted_ids, tile_ranges, final_T,
-                               n_contrib, stream);
+                               n_contrib, false, stream);
 }
 
 }  // namespace gs

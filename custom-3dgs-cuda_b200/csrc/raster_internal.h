@@ -12,9 +12,10 @@ void fill_bin_params(BinParams& bp, const RasterLayout& L, char* ws, int N, int 
                      const float* colors, const float* alpha, long long capacity);
 
 // Enqueues everything after binning prep: depth sort, pair duplication, tile sort, tile
-// ranges and the forward blend.
+// ranges and the forward blend (the throughput variant when `throughput`, see blend.cuh).
 int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
                           long long capacity, float* img, int* sorted_ids, int* tile_ranges,
-                          float* final_T, int* n_contrib, cudaStream_t stream);
+                          float* final_T, int* n_contrib, bool throughput,
+                          cudaStream_t stream);
 
 }  // namespace gs

@@ -246,7 +246,8 @@ extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const flo
                                  int* pair_count_host, void* m_ready_event, unsigned flags,
                                  void* stream) {
   GS_API_BEGIN();
-  GS_REQUIRE((flags & ~GS_RENDER_TIGHT_BINS) == 0u, "unknown render flag");
+  GS_REQUIRE((flags & ~(GS_RENDER_TIGHT_BINS | GS_RENDER_CONCURRENT)) == 0u,
+             "unknown render flag");
   GS_REQUIRE(N >= 0, "N must be non-negative");
   GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
   GS_REQUIRE((W + 15) / 16 < 65536 && (H + 15) / 16 < 65536, "image too large");
@@ -299,7 +300,8 @@ extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const flo
                             cudaMemcpyDeviceToHost, st));
   if (m_ready_event) GS_CUDA(cudaEventRecord((cudaEvent_t)m_ready_event, st));
   return launch_sort_and_blend(L, N, H, W, ws, pair_capacity, img, sorted_ids, tile_ranges,
-                               final_T, n_contrib, st);
+                               final_T, n_contrib,
+                               (flags & GS_RENDER_CONCURRENT) != 0u, st);
   GS_API_END();
 }
 
@@ -320,8 +322,9 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
                                   float* g_mean2d, int accumulate, float* stat_norm_sum,
                                   float* stat_count, float* stat_max, float stat_scale_x,
                                   float stat_scale_y, void* accum_wait_event,
-                                  void* accum_done_event, void* stream) {
+                                  void* accum_done_event, unsigned flags, void* stream) {
   GS_API_BEGIN();
+  GS_REQUIRE((flags & ~GS_RENDER_CONCURRENT) == 0u, "unknown render backward flag");
   GS_REQUIRE(N >= 0, "N must be non-negative");
   GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
   if (N == 0) return GS_OK;
@@ -353,8 +356,13 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
   bp.n_contrib = n_contrib;
   bp.g_mean2d = bp.g_cov2d = bp.g_colors = bp.g_alpha = nullptr;
   bp.g_accum = accum;
-  blend_backward_kernel<true, kBlendBwdPix>
-      <<<(unsigned)L.T, kTilePixels / kBlendBwdPix, 0, st>>>(bp);
+  if (flags & GS_RENDER_CONCURRENT) {
+    blend_backward_kernel<true, kBlendBwdPixThroughput>
+        <<<(unsigned)L.T, kTilePixels / kBlendBwdPixThroughput, 0, st>>>(bp);
+  } else {
+    blend_backward_kernel<true, kBlendBwdPix>
+        <<<(unsigned)L.T, kTilePixels / kBlendBwdPix, 0, st>>>(bp);
+  }
   GS_CHECK_LAUNCH();
   mark_stage(8, st);
   GaussianBwdParams gp;

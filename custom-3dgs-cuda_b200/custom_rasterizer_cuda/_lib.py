@@ -49,7 +49,7 @@ SIGNATURES = {
     "gs_render_backward": (c_int, [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, c_float,
                                    c_float, c_float, c_float, P, c_longlong, P, P, P, P, P,
                                    c_size_t, P, P, P, P, P, P, P, c_int, P, P, P, c_float,
-                                   c_float, P, P, P]),
+                                   c_float, P, P, c_uint, P]),
     "gs_l1_ssim_workspace_size": (c_size_t, [c_int, c_int]),
     "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),

@@ -28,13 +28,16 @@ class RenderState:
     n_contrib: torch.Tensor
     height: int
     width: int
+    backward_flags: int = 0    # GS_RENDER_CONCURRENT when the forward was given it
 
 
 def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy, height,
-                   width, tight_bins: bool = False):
+                   width, tight_bins: bool = False, concurrent: bool = False):
     """(img[H,W,3], radii[N], RenderState). `opacity` is post-sigmoid, N or [N,1].
     tight_bins: bin splats only into tiles where they can pass the opacity test (same image
-    and gradients, shorter tile lists; the state's lists then differ from the reference's)."""
+    and gradients, shorter tile lists; the state's lists then differ from the reference's).
+    concurrent: the caller overlaps several views on streams; the blend kernels (this one and
+    the state's backward) use their throughput variants (GS_RENDER_CONCURRENT)."""
     N, H, W = int(mu.shape[0]), int(height), int(width)
     dev = mu.device
     T = _tiles(H, W)
@@ -46,6 +49,7 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
     tile_ranges = torch.empty((T, 2), **i32)
     radii = torch.empty((N,), **f32)
     mode = 1 if tight_bins else 0
+    flags = mode | (2 if concurrent else 0)
     cap = _capacity.guess(N, H, W, mode)
     with torch.cuda.device(dev):
         stream = _stream(dev)
@@ -60,12 +64,13 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
                 _ptr(R), _ptr(t), _ptr(cam_pos), float(fx), float(fy), float(cx), float(cy),
                 ws.data_ptr(), ws_bytes, cap, _ptr(img), sorted_ids.data_ptr(),
                 _ptr(tile_ranges), _ptr(final_T), _ptr(n_contrib), _ptr(radii),
-                m_host.data_ptr(), ev.handle, mode, stream))
+                m_host.data_ptr(), ev.handle, flags, stream))
             ev.synchronize()
             M = int(m_host[0])
             _capacity.update(N, H, W, M, mode)
             if M <= cap:
-                state = RenderState(ws, cap, sorted_ids, M, tile_ranges, final_T, n_contrib, H, W)
+                state = RenderState(ws, cap, sorted_ids, M, tile_ranges, final_T, n_contrib, H, W,
+                                    flags & 2)
                 return img, radii, state
             cap = M
     raise RuntimeError("pair count kept growing between attempts")
@@ -107,5 +112,5 @@ def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, c
               if stats is not None else (None, None, None, 0.0, 0.0)),
             accum_wait.handle if accum_wait is not None else None,
             accum_done.handle if accum_done is not None else None,
-            _stream(dev)))
+            state.backward_flags, _stream(dev)))
     return (*out, g_mean2d)

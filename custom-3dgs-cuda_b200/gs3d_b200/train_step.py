@@ -183,9 +183,10 @@ class Trainer:
     view's parameter gradients are added straight into the flat bucket, the densification
     statistics are updated inside the per-Gaussian backward kernel and the opacity gradient is
     taken through the sigmoid once per step. Consecutive views run on `view_streams`
-    alternating CUDA streams (1 = all on the current stream), and with `tight_bins` the splats
-    are binned only into tiles where they can pass the opacity test (same images and
-    gradients, shorter tile lists). mode "autograd" runs the same step through
+    alternating CUDA streams (1 = all on the current stream), the blend kernels then in their
+    throughput variants (GS_RENDER_CONCURRENT), and with `tight_bins` the splats are binned
+    only into tiles where they can pass the opacity test (same images and gradients, shorter
+    tile lists). mode "autograd" runs the same step through
     `gaussian_splatting.rasterizer.rasterize` (the drop-in RasterizeFunction) and
     loss.backward(), as the reference trainer does.
     """
@@ -248,6 +249,9 @@ class Trainer:
             with torch.cuda.device(device):
                 self._streams = [torch.cuda.Stream(device) for _ in range(view_streams)]
                 self._accum_events = [_lib.Event(), _lib.Event()]
+        # views overlap on streams: the blend kernels' throughput variants (also in steps
+        # whose views run in order, so that per-stage timings see the same kernels)
+        self.concurrent_views = len(self._streams) > 1
 
     def _update(self) -> None:
         """Batch-mean gradients across ranks, then Adam. The sharded step does both (and the
@@ -306,7 +310,8 @@ class Trainer:
                 with torch.cuda.stream(st):
                     img, _, rs = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
                                                 v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
-                                                v["width"], tight_bins=self.tight_bins)
+                                                v["width"], tight_bins=self.tight_bins,
+                                                concurrent=self.concurrent_views)
                     target = targets.get(vi) if staged else targets[vi]
                     loss, gimg = l1_ssim_value_and_grad(img, target, LAMBDA_DSSIM)
                     if staged:

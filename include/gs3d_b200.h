@@ -157,7 +157,8 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
  * and where n > 0, stat_norm_sum += n, stat_count += 1, stat_max = max(stat_max, n).
  * accum_wait_event / accum_done_event (cudaEvent_t or NULL): the kernel that writes the gradient
  * and statistic buffers waits for the first and the second is recorded after it, so that views
- * rendered concurrently on several streams can accumulate into the same buffers.
+ * rendered concurrently on several streams can accumulate into the same buffers. flags: 0 or
+ * GS_RENDER_CONCURRENT.
  */
 /* gs_render_forward flags. GS_RENDER_TIGHT_BINS: bin each splat only into the tiles of its
  * reference rectangle that hold a pixel of its opacity-test extent box (the region where
@@ -166,6 +167,12 @@ GS_API int gs_project_backward(int N, const float* g_mean2d, const float* g_cov2
  * pixel of their tile; M is smaller, so sorted_ids, tile_ranges and n_contrib (a list position)
  * differ from the reference's. Without the flag all outputs match the reference's. */
 #define GS_RENDER_TIGHT_BINS 1u
+/* GS_RENDER_CONCURRENT (gs_render_forward and gs_render_backward): the caller overlaps several
+ * views on different streams. The blend kernels then run with more pixels per thread (2 forward,
+ * 4 backward instead of 1 and 2): fewer instructions per pixel, which raises throughput when
+ * other kernels share the SMs, at the cost of a longer kernel when it runs alone. The forward
+ * outputs are identical; the gradients differ only in the order of their float sums. */
+#define GS_RENDER_CONCURRENT 2u
 
 GS_API size_t gs_render_workspace_size(int N, int H, int W, long long pair_capacity);
 GS_API int gs_render_forward(int N, int H, int W, const float* mu, const float* q, const float* s,
@@ -188,7 +195,8 @@ GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const 
                               float* g_opacity, float* g_albedo, float* g_k_j, float* g_mean2d,
                               int accumulate, float* stat_norm_sum, float* stat_count,
                               float* stat_max, float stat_scale_x, float stat_scale_y,
-                              void* accum_wait_event, void* accum_done_event, void* stream);
+                              void* accum_wait_event, void* accum_done_event, unsigned flags,
+                              void* stream);
 
 /*
  * Fused photometric loss of the training step (no counterpart in the reference's extension;

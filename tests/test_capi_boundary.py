@@ -102,7 +102,8 @@ def test_python_boundary_checks_match_reference_messages():
 
 
 def test_training_entry_points_reject_bad_arguments_before_cuda():
-    """gs_adam_step, gs_sharded_adam_step and gs_render_forward validate on the host."""
+    """gs_adam_step, gs_sharded_adam_step, gs_render_forward and gs_render_backward validate
+    on the host."""
     from custom_rasterizer_cuda import _lib
 
     L = _lib.lib
@@ -135,4 +136,9 @@ def test_training_entry_points_reject_bad_arguments_before_cuda():
     # unknown render flag
     assert L.gs_render_forward(1, 16, 16, *([16] * 9), 1.0, 1.0, 8.0, 8.0, 256, 1 << 20, 16,
                                *([256] * 6), None, None, 0x80, None) == _lib.GS_ERR_INVALID_ARG
+    assert b"flag" in L.gs_last_error()
+    # the backward takes GS_RENDER_CONCURRENT only
+    assert L.gs_render_backward(1, 16, 16, *([16] * 9), 1.0, 1.0, 8.0, 8.0, 256, 1 << 20,
+                                *([256] * 4), 256, 1 << 20, *([256] * 7), 0, None, None, None,
+                                1.0, 1.0, None, None, 1, None) == _lib.GS_ERR_INVALID_ARG
     assert b"flag" in L.gs_last_error()

@@ -35,8 +35,10 @@ def op_chain(crc, sc, view, dev, grad_img):
                 grads=(gmu + gmu_sh, gq, gs, ga.reshape(-1), gA, gkj), mean2d_grad=gm)
 
 
+@pytest.mark.parametrize("concurrent", [False, True], ids=["latency", "throughput"])
 @pytest.mark.parametrize("case", list(scenes_small()), ids=lambda c: c[0])
-def test_fused_render_matches_op_chain(crc, cuda_device, case):
+def test_fused_render_matches_op_chain(crc, cuda_device, case, concurrent):
+    """Both blend variants (GS_RENDER_CONCURRENT selects the throughput one)."""
     from custom_rasterizer_cuda.render import render_backward, render_forward
 
     _, sc, view = case
@@ -49,7 +51,8 @@ def test_fused_render_matches_op_chain(crc, cuda_device, case):
     cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
     op = torch.sigmoid(al).contiguous()
     img, radii, st = render_forward(mu, q, s, op, A, kj, R, t, cam, view.fx, view.fy, view.cx,
-                                    view.cy, view.height, view.width)
+                                    view.cy, view.height, view.width, concurrent=concurrent)
+    assert st.backward_flags == (2 if concurrent else 0)
     assert torch.equal(img, ref["img"])
     assert torch.equal(st.final_T, ref["final_T"]) and torch.equal(st.n_contrib, ref["n_contrib"])
     assert torch.equal(st.sorted_ids[:st.pairs], ref["ids"])
