@@ -63,11 +63,32 @@ struct BlendGeometry {
   }
 };
 
-// Warp-uniform test: can splat record r0 = (mean, extent) reach the warp's pixel block?
+// Can splat record (r0 = (mean, extent), r1 = (conic, opacity)) reach the warp's pixel block
+// (pixel centres [wx0, wx0 + 7] x [wy0, wy0 + 4 kPix - 1])? First its extent box, then its
+// opacity ellipse: a pixel passes the opacity test only where Q(d) = d^T conic d <=
+// tau = 2 ln(255 o), so the block is reachable only if the minimum of Q over the block's
+// rectangle (offsets d from the mean) is at most tau. Q is convex with its minimum at d = 0,
+// so the rectangle's minimum lies on an edge that faces the mean (or is 0 when the mean is
+// inside): one candidate per axis, the clamped line minimum on the edge nearest the mean,
+// and the smaller of the two is the minimum. The test is conservative: tau is inflated as the
+// extent is (1% + 1e-3) and a degenerate conic falls back to the box.
 template <int kPix>
-__device__ __forceinline__ bool warp_block_hit(float4 r0, float wx0, float wy0) {
-  return r0.x + r0.z >= wx0 && r0.x - r0.z <= wx0 + 7.0f && r0.y + r0.w >= wy0 &&
-         r0.y - r0.w <= wy0 + (4.0f * kPix - 1.0f);
+__device__ __forceinline__ bool warp_block_hit(float4 r0, float4 r1, float wx0, float wy0) {
+  constexpr float kSpanY = 4.0f * kPix - 1.0f;
+  if (!(r0.x + r0.z >= wx0 && r0.x - r0.z <= wx0 + 7.0f && r0.y + r0.w >= wy0 &&
+        r0.y - r0.w <= wy0 + kSpanY))
+    return false;
+  const float a = r1.x, b = r1.y, c = r1.z;
+  if (!(a > 0.0f && c > 0.0f && a * c > b * b)) return true;
+  const float x0 = wx0 - r0.x, x1 = x0 + 7.0f, y0 = wy0 - r0.y, y1 = y0 + kSpanY;
+  const float X = fminf(fmaxf(0.0f, x0), x1);  // the edge (or centre column) nearest the mean
+  const float Y = fminf(fmaxf(0.0f, y0), y1);
+  const float yX = fminf(fmaxf(__fdividef(-b * X, c), y0), y1);  // line minimum on x = X
+  const float xY = fminf(fmaxf(__fdividef(-b * Y, a), x0), x1);  // line minimum on y = Y
+  const float qX = fmaf(a * X, X, fmaf(2.0f * b * X, yX, c * yX * yX));
+  const float qY = fmaf(a * xY, xY, fmaf(2.0f * b * xY, Y, c * Y * Y));
+  const float tau = 2.0f * __logf(255.0f * r1.w);
+  return fminf(qX, qY) <= fmaf(tau, 1.01f, 1e-3f);
 }
 
 struct BlendFwdParams {
@@ -87,8 +108,8 @@ struct BlendFwdParams {
 // alpha = min(0.99, o * exp(power)), skipped when power > 0 or alpha < 1/255; colour
 // accumulates c * alpha * T and T *= 1 - alpha; the pixel stops after the Gaussian that
 // takes T below 1e-4. n_contrib is the 1-based list position of the last Gaussian applied.
-// A warp skips splats whose extent box misses its pixel block (warp_block_hit): those fail
-// the opacity test at every pixel of the block, so the outputs are unchanged.
+// A warp skips splats whose opacity ellipse misses its pixel block (warp_block_hit): those
+// fail the opacity test at every pixel of the block, so the outputs are unchanged.
 template <int kPix>
 static __global__ void __launch_bounds__(kTilePixels / kPix)
     blend_forward_kernel(BlendFwdParams p) {
@@ -151,7 +172,8 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
     // walks the hits in list order (pixels that are done skip them)
     for (int k = 0; k < n && !__all_sync(0xffffffffu, all_done); k += 32) {
       const int i_lane = k + lane;
-      const bool hit = i_lane < n && warp_block_hit<kPix>(rec[0][i_lane], geo.wx0, geo.wy0);
+      const bool hit =
+          i_lane < n && warp_block_hit<kPix>(rec[0][i_lane], rec[1][i_lane], geo.wx0, geo.wy0);
       unsigned hits = __ballot_sync(0xffffffffu, hit);
       while (hits) {
         const int i = k + __ffs(hits) - 1;
@@ -262,8 +284,8 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // Gaussians back to front from its n_contrib, recovering T before each one as
 // T / max(1 - alpha, 1e-4), and produces dL/d(mean, conic, colour, opacity). The tile
 // walk starts at the batch holding the tile's largest n_contrib instead of the list end;
-// each warp starts at its own largest n_contrib and skips splats whose extent box misses its
-// pixel block (exact: they fail the opacity test there). Per Gaussian, the contributions of a
+// each warp starts at its own largest n_contrib and skips splats whose opacity ellipse misses
+// its pixel block (warp_block_hit; exact: they fail the opacity test there). Per Gaussian, the contributions of a
 // thread's pixels are summed, reduced per warp (warp_reduce9) and added into a per-batch shared
 // slot; after each batch the slot sums are flushed to the global gradients.
 //
@@ -373,7 +395,8 @@ __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinB
     for (int top = min(hi, warp_last); top > lo; top -= 32) {
       const int j_lane = top - 1 - lane;
       const bool hit =
-          j_lane >= lo && warp_block_hit<kPix>(rec[0][j_lane - lo], geo.wx0, geo.wy0);
+          j_lane >= lo &&
+          warp_block_hit<kPix>(rec[0][j_lane - lo], rec[1][j_lane - lo], geo.wx0, geo.wy0);
       unsigned hits = __ballot_sync(0xffffffffu, hit);
       while (hits) {
         const int j = top - __ffs(hits);
