@@ -91,6 +91,65 @@ __device__ __forceinline__ bool warp_block_hit(float4 r0, float4 r1, float wx0, 
   return fminf(qX, qY) <= fmaf(tau, 1.01f, 1e-3f);
 }
 
+__device__ __forceinline__ float approx_sqrt(float x) {
+  float y;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Which rows of the warp's pixel block (pixel centres [wx0, wx0 + 7] x [wy0, wy0 + 4 kPix - 1])
+// can splat record (r0 = (mean, extent), r1 = (conic, opacity)) reach? Bit q of the result
+// stands for the 8 x 4 sub-block of rows [4q, 4q + 3], the pixels q of the warp's threads;
+// 0 means the splat misses the block. A pixel passes the opacity test only where
+// Q(d) = d^T conic d <= tau = 2 ln(255 o) (d: offset from the mean), an ellipse. Past the extent
+// box test, the ellipse's y-range over the block's column band x in [x0, x1] is exact by
+// convexity: the top of the band's slice is the ellipse's upper boundary at the band point
+// nearest the ellipse's topmost point (clamped), the bottom likewise at the bottommost point.
+// The test is conservative: tau is inflated as the extent is (1% + 1e-3), the range widened by
+// 0.05 px, and a degenerate conic keeps the extent box.
+template <int kPix>
+__device__ __forceinline__ unsigned warp_block_reach(float4 r0, float4 r1, float wx0, float wy0) {
+  constexpr float kSpanY = 4.0f * kPix - 1.0f;
+  if (!(r0.x + r0.z >= wx0 && r0.x - r0.z <= wx0 + 7.0f && r0.y + r0.w >= wy0 &&
+        r0.y - r0.w <= wy0 + kSpanY))
+    return 0u;
+  const float y0 = wy0 - r0.y;
+  float lo = -r0.w - y0, hi = r0.w - y0;  // reached rows, relative to wy0 (extent box)
+  const float a = r1.x, b = r1.y, c = r1.z;
+  const float det = a * c - b * b;
+  if (a > 0.0f && c > 0.0f && det > 0.0f) {
+    const float x0 = wx0 - r0.x, x1 = x0 + 7.0f;
+    const float tau = fmaf(2.0f * __logf(255.0f * r1.w), 1.01f, 1e-3f);
+    const float ct = c * tau;
+    const float yt = approx_sqrt(fmaxf(__fdividef(tau * a, det), 0.0f));  // topmost point
+    const float xt = __fdividef(-b * yt, a);
+    const float xa = fminf(fmaxf(xt, x0), x1), xb = fminf(fmaxf(-xt, x0), x1);
+    const float inv_c = __fdividef(1.0f, c);
+    const float ya = (-b * xa + approx_sqrt(fmaxf(fmaf(-det * xa, xa, ct), 0.0f))) * inv_c;
+    const float yb = (-b * xb - approx_sqrt(fmaxf(fmaf(-det * xb, xb, ct), 0.0f))) * inv_c;
+    lo = fmaxf(lo, yb - 0.05f - y0);
+    hi = fminf(hi, ya + 0.05f - y0);
+  }
+  if (!(hi >= 0.0f && lo <= kSpanY && lo <= hi)) return 0u;
+  // sub-block q is reached iff hi >= 4q and lo <= 4q + 3
+  const int q_hi = min((int)(fminf(hi, kSpanY) * 0.25f), kPix - 1);
+  const int q_lo = max((int)ceilf((fmaxf(lo, -4.0f) - 3.0f) * 0.25f), 0);
+  if (q_lo > q_hi) return 0u;
+  return ((2u << q_hi) - 1u) & ~((1u << q_lo) - 1u);
+}
+
+// Rows of the block a record reaches (bit q: pixels q of the warp's threads). With four
+// pixels per thread the per-row mask pays for its cost (40% of the row groups of a hit block
+// are missed at config 4); with one or two the plain block test is cheaper.
+template <int kPix>
+__device__ __forceinline__ unsigned warp_block_rows(float4 r0, float4 r1, float wx0, float wy0) {
+  if constexpr (kPix >= 4) {
+    return warp_block_reach<kPix>(r0, r1, wx0, wy0);
+  } else {
+    return warp_block_hit<kPix>(r0, r1, wx0, wy0) ? (1u << kPix) - 1u : 0u;
+  }
+}
+
 struct BlendFwdParams {
   int W, H, tiles_x;
   const int2* ranges;
@@ -108,7 +167,8 @@ struct BlendFwdParams {
 // alpha = min(0.99, o * exp(power)), skipped when power > 0 or alpha < 1/255; colour
 // accumulates c * alpha * T and T *= 1 - alpha; the pixel stops after the Gaussian that
 // takes T below 1e-4. n_contrib is the 1-based list position of the last Gaussian applied.
-// A warp skips splats whose opacity ellipse misses its pixel block (warp_block_hit): those
+// A warp skips splats whose opacity ellipse misses its pixel block, and the pixels q of its
+// threads skip splats that miss their rows of the block (warp_block_rows): those
 // fail the opacity test at every pixel of the block, so the outputs are unchanged.
 template <int kPix>
 static __global__ void __launch_bounds__(kTilePixels / kPix)
@@ -172,17 +232,22 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
     // walks the hits in list order (pixels that are done skip them)
     for (int k = 0; k < n && !__all_sync(0xffffffffu, all_done); k += 32) {
       const int i_lane = k + lane;
-      const bool hit =
-          i_lane < n && warp_block_hit<kPix>(rec[0][i_lane], rec[1][i_lane], geo.wx0, geo.wy0);
-      unsigned hits = __ballot_sync(0xffffffffu, hit);
+      const unsigned reach =
+          i_lane < n ? warp_block_rows<kPix>(rec[0][i_lane], rec[1][i_lane], geo.wx0, geo.wy0)
+                     : 0u;
+      unsigned hits = __ballot_sync(0xffffffffu, reach != 0u);
       while (hits) {
-        const int i = k + __ffs(hits) - 1;
+        const int src = __ffs(hits) - 1;
+        const int i = k + src;
         hits &= hits - 1;
+        const unsigned rows =  // warp-uniform
+            kPix >= 4 ? __shfl_sync(0xffffffffu, reach, src) : (1u << kPix) - 1u;
         const float4 r0 = rec[0][i];
         const float4 r1 = rec[1][i];
         const float dx = fpx - r0.x;
 #pragma unroll
         for (int q = 0; q < kPix; ++q) {
+          if (!((rows >> q) & 1u)) continue;  // the splat misses these rows of the block
           if (done[q]) continue;
           const float dy = fpy[q] - r0.y;
           const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
@@ -285,7 +350,8 @@ constexpr int kAccStride = 10;  // 9 gradient sums per batch slot, padded
 // T / max(1 - alpha, 1e-4), and produces dL/d(mean, conic, colour, opacity). The tile
 // walk starts at the batch holding the tile's largest n_contrib instead of the list end;
 // each warp starts at its own largest n_contrib and skips splats whose opacity ellipse misses
-// its pixel block (warp_block_hit; exact: they fail the opacity test there). Per Gaussian, the contributions of a
+// its pixel block and each pixel row group q the splats that miss its rows (warp_block_rows;
+// exact: they fail the opacity test there). Per Gaussian, the contributions of a
 // thread's pixels are summed, reduced per warp (warp_reduce9) and added into a per-batch shared
 // slot; after each batch the slot sums are flushed to the global gradients.
 //
@@ -394,13 +460,17 @@ __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinB
     // the warp's pixel block, the warp walks the hits back to front
     for (int top = min(hi, warp_last); top > lo; top -= 32) {
       const int j_lane = top - 1 - lane;
-      const bool hit =
-          j_lane >= lo &&
-          warp_block_hit<kPix>(rec[0][j_lane - lo], rec[1][j_lane - lo], geo.wx0, geo.wy0);
-      unsigned hits = __ballot_sync(0xffffffffu, hit);
+      const unsigned reach =
+          j_lane >= lo
+              ? warp_block_rows<kPix>(rec[0][j_lane - lo], rec[1][j_lane - lo], geo.wx0, geo.wy0)
+              : 0u;
+      unsigned hits = __ballot_sync(0xffffffffu, reach != 0u);
       while (hits) {
-        const int j = top - __ffs(hits);
+        const int src = __ffs(hits) - 1;
+        const int j = top - 1 - src;
         hits &= hits - 1;
+        const unsigned rows =  // warp-uniform
+            kPix >= 4 ? __shfl_sync(0xffffffffu, reach, src) : (1u << kPix) - 1u;
         const int k = j - lo;  // slot in this batch
         const float4 r0 = rec[0][k];
         float v[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -412,6 +482,7 @@ __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinB
         const float dx = fpx - r0.x;
 #pragma unroll
         for (int q = 0; q < kPix; ++q) {
+          if (!((rows >> q) & 1u)) continue;  // the splat misses these rows of the block
           if (j >= last[q]) continue;  // contributor j + 1 > n_contrib of this pixel
           const float dy = fpy[q] - r0.y;
           const float power = splat_power(make_float3(r1.x, r1.y, r1.z), dx, dy);
