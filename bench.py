@@ -372,10 +372,11 @@ def view_pair_stats(trainer, views: list[dict]) -> dict:
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each stage's kernel,
 # from one `ncu --set full --clock-control none` capture of a config-2 view (1M Gaussians of
-# the config-4 distribution at 1920x1080: `bench.py --view-only --steps 1 --warmup 1`).
+# the config-4 distribution at 1920x1080) with the training step's kernels:
+# `bench.py --view-only --view-throughput --steps 1 --warmup 1`.
 NCU_DRAM_BYTES = {
-    "preprocess": 259.1e6, "duplicate": 14.7e6, "blend_forward": 74.2e6,
-    "blend_backward": 142.4e6, "gaussian_backward": 489.7e6,
+    "preprocess": 284.1e6, "duplicate": 12.2e6, "blend_forward": 67.5e6,
+    "blend_backward": 135.9e6, "gaussian_backward": 497.9e6,
 }
 
 
@@ -499,11 +500,14 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-render-table", action="store_true",
                     help="skip the per-scene forward/backward/FPS table (configs 1-3)")
-    ap.add_argument("--view-streams", type=int, default=3,
+    ap.add_argument("--view-streams", type=int, default=6,
                     help="CUDA streams the views of a step alternate over (1 = in order)")
     ap.add_argument("--view-only", action="store_true",
                     help="forward+backward of one config-2 view per step (single GPU); a small "
                          "fixed workload for profiler captures of single kernels")
+    ap.add_argument("--view-throughput", action="store_true",
+                    help="with --view-only: the training step's kernel variants (tight bins, "
+                         "GS_RENDER_CONCURRENT blend kernels) instead of the single-view ones")
     ap.add_argument("--table-only", action="store_true",
                     help="only the per-scene forward/backward/FPS table (single GPU)")
     ap.add_argument("--table-scenes", default=None,
@@ -551,7 +555,9 @@ def run_view(args) -> int:
         if k >= args.warmup:
             timer.install_next()
         img, _, st = render_forward(mu, q, s, op, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
-                                    v["cx"], v["cy"], v["height"], v["width"])
+                                    v["cx"], v["cy"], v["height"], v["width"],
+                                    tight_bins=args.view_throughput,
+                                    concurrent=args.view_throughput)
         render_backward(st, grad_img, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"], v["fy"],
                         v["cx"], v["cy"], want_mean2d_grad=False)
     torch.cuda.synchronize()
@@ -559,6 +565,8 @@ def run_view(args) -> int:
     if _lib.device_error_bits() != 0:
         raise RuntimeError(f"device error bits {_lib.device_error_bits():#x}")
     emit({"mode": "view", "workload": "config2 view 0: 1M Gaussians, 1920x1080",
+          "kernels": ("training-step variants (tight bins, throughput blend kernels)"
+                      if args.view_throughput else "reference binning, latency blend kernels"),
           "steps": args.steps, "warmup": args.warmup, "pairs": st.pairs,
           "stage_ms": timer.stage_ms()})
     return 0

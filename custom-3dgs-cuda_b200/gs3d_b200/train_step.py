@@ -193,7 +193,7 @@ class Trainer:
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
                  fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct",
-                 view_streams: int = 3, tight_bins: bool = True):
+                 view_streams: int = 6, tight_bins: bool = True):
         from gaussian_splatting.scene.gaussian import gaussian
 
         self.device = device
