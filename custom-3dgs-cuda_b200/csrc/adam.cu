@@ -7,7 +7,9 @@
 // Gradients come from one flat buffer and the moments live in flat buffers of the same
 // layout, so a group's slice is contiguous everywhere; each CTA updates float4 chunks of one
 // group (parameters, gradients and both moments read once and written once: 28 bytes per
-// element of HBM traffic).
+// element of HBM traffic). A group may carry clamp bounds applied to the updated parameter in
+// the same pass, as the reference trainer clamps the opacity logits and log-scales right after
+// optimizer.step() (scripts/train.py:171-178): p = min(max(p, lo), hi).
 #include <cmath>
 
 #include "capi_internal.h"
@@ -27,6 +29,8 @@ struct AdamParams {
   long long size[kAdamMaxGroups];
   unsigned block_start[kAdamMaxGroups + 1];
   float step_size[kAdamMaxGroups];      // lr / (1 - b1^t)
+  float clamp_lo[kAdamMaxGroups], clamp_hi[kAdamMaxGroups];
+  unsigned clamp_mask;                  // bit k: group k is clamped
   float bc2_sqrt;                       // sqrt(1 - b2^t)
   float beta1, beta2, one_minus_beta1, one_minus_beta2, eps;  // 1 - beta formed in double
   const float* grad;
@@ -35,11 +39,12 @@ struct AdamParams {
 };
 
 __device__ __forceinline__ float adam_one(float& p, float g, float& m, float& v, float step_size,
-                                          const AdamParams& a) {
+                                          const AdamParams& a, bool clamp, float lo, float hi) {
   m = m + a.one_minus_beta1 * (g - m);  // the lerp form torch uses
   v = a.beta2 * v + a.one_minus_beta2 * g * g;
   const float denom = sqrtf(v) / a.bc2_sqrt + a.eps;
   p -= step_size * (m / denom);
+  if (clamp) p = fminf(fmaxf(p, lo), hi);
   return p;
 }
 
@@ -55,6 +60,8 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(AdamParams a) {
   float* __restrict__ m = a.exp_avg + a.offset[grp];
   float* __restrict__ v = a.exp_avg_sq + a.offset[grp];
   const float step_size = a.step_size[grp];
+  const bool clamp = (a.clamp_mask >> grp) & 1u;
+  const float lo = a.clamp_lo[grp], hi = a.clamp_hi[grp];
   // float4 path when every slice of the group is 16-byte aligned
   const bool vec = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
                      reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
@@ -67,17 +74,17 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(AdamParams a) {
       const float4 gg = __ldg(reinterpret_cast<const float4*>(g + i));
       float4 mm = *reinterpret_cast<float4*>(m + i);
       float4 vv = *reinterpret_cast<float4*>(v + i);
-      adam_one(pp.x, gg.x, mm.x, vv.x, step_size, a);
-      adam_one(pp.y, gg.y, mm.y, vv.y, step_size, a);
-      adam_one(pp.z, gg.z, mm.z, vv.z, step_size, a);
-      adam_one(pp.w, gg.w, mm.w, vv.w, step_size, a);
+      adam_one(pp.x, gg.x, mm.x, vv.x, step_size, a, clamp, lo, hi);
+      adam_one(pp.y, gg.y, mm.y, vv.y, step_size, a, clamp, lo, hi);
+      adam_one(pp.z, gg.z, mm.z, vv.z, step_size, a, clamp, lo, hi);
+      adam_one(pp.w, gg.w, mm.w, vv.w, step_size, a, clamp, lo, hi);
       *reinterpret_cast<float4*>(p + i) = pp;
       *reinterpret_cast<float4*>(m + i) = mm;
       *reinterpret_cast<float4*>(v + i) = vv;
     } else {
       for (long long j = i; j < i + kAdamVec && j < size; ++j) {
         float pj = p[j], mj = m[j], vj = v[j];
-        adam_one(pj, g[j], mj, vj, step_size, a);
+        adam_one(pj, g[j], mj, vj, step_size, a, clamp, lo, hi);
         p[j] = pj;
         m[j] = mj;
         v[j] = vj;
@@ -93,7 +100,7 @@ using namespace gs;
 extern "C" int gs_adam_step(int n_groups, float* const* params, const long long* sizes,
                             const float* lrs, const float* grad, float* exp_avg,
                             float* exp_avg_sq, double beta1, double beta2, double eps, long long step,
-                            void* stream) {
+                            const float* clamp_min, const float* clamp_max, void* stream) {
   GS_API_BEGIN();
   GS_REQUIRE(n_groups >= 0 && n_groups <= kAdamMaxGroups, "n_groups must be in [0, 8]");
   GS_REQUIRE(step >= 1, "step must be >= 1");
@@ -118,6 +125,10 @@ extern "C" int gs_adam_step(int n_groups, float* const* params, const long long*
     off += sizes[k];
     const double bc1 = 1.0 - std::pow(beta1, (double)step);
     a.step_size[k] = (float)((double)lrs[k] / bc1);
+    a.clamp_lo[k] = clamp_min ? clamp_min[k] : -INFINITY;
+    a.clamp_hi[k] = clamp_max ? clamp_max[k] : INFINITY;
+    GS_REQUIRE(!(a.clamp_lo[k] > a.clamp_hi[k]), "clamp_min above clamp_max");
+    if (a.clamp_lo[k] > -INFINITY || a.clamp_hi[k] < INFINITY) a.clamp_mask |= 1u << k;
   }
   for (int k = n_groups; k < kAdamMaxGroups; ++k) a.block_start[k] = blocks;
   a.block_start[kAdamMaxGroups] = blocks;

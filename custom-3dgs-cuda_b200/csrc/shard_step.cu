@@ -37,6 +37,8 @@ struct ShardArgs {
   int n_groups;
   long long group_end[kShardMaxGroups];  // exclusive end of each parameter group
   float step_size[kShardMaxGroups];
+  float clamp_lo[kShardMaxGroups], clamp_hi[kShardMaxGroups];
+  unsigned clamp_mask;  // bit k: group k's parameters are clamped after the update
   float bc2_sqrt, beta1, beta2, one_minus_beta1, one_minus_beta2, eps, grad_scale;
 };
 
@@ -146,6 +148,7 @@ __device__ __forceinline__ void adam_lane(const ShardArgs& a, long long idx, flo
   v = a.beta2 * v + a.one_minus_beta2 * g * g;
   const float denom = sqrtf(v) / a.bc2_sqrt + a.eps;
   p -= a.step_size[grp] * (m / denom);
+  if ((a.clamp_mask >> grp) & 1u) p = fminf(fmaxf(p, a.clamp_lo[grp]), a.clamp_hi[grp]);
 }
 
 __device__ __forceinline__ void mark_phase(const gs_shard_buffers& b, int k) {
@@ -263,7 +266,8 @@ using namespace gs;
 extern "C" int gs_sharded_adam_step(const gs_shard_buffers* bufs, float* exp_avg,
                                     float* exp_avg_sq, int n_groups, const long long* group_sizes,
                                     const float* lrs, double beta1, double beta2, double eps,
-                                    long long step, float grad_scale, void* stream) {
+                                    long long step, float grad_scale, const float* clamp_min,
+                                    const float* clamp_max, void* stream) {
   GS_API_BEGIN();
   GS_REQUIRE(bufs, "null buffer description");
   const gs_shard_buffers& b = *bufs;
@@ -301,6 +305,10 @@ extern "C" int gs_sharded_adam_step(const gs_shard_buffers* bufs, float* exp_avg
     end += group_sizes[k];
     a.group_end[k] = end;
     a.step_size[k] = (float)((double)lrs[k] / bc1);
+    a.clamp_lo[k] = clamp_min ? clamp_min[k] : -INFINITY;
+    a.clamp_hi[k] = clamp_max ? clamp_max[k] : INFINITY;
+    GS_REQUIRE(!(a.clamp_lo[k] > a.clamp_hi[k]), "clamp_min above clamp_max");
+    if (a.clamp_lo[k] > -INFINITY || a.clamp_hi[k] < INFINITY) a.clamp_mask |= 1u << k;
   }
   GS_REQUIRE(end == b.n_param, "group sizes must add up to n_param");
   a.bc2_sqrt = (float)std::sqrt(1.0 - std::pow(beta2, (double)step));

@@ -53,9 +53,10 @@ SIGNATURES = {
     "gs_l1_ssim_workspace_size": (c_size_t, [c_int, c_int]),
     "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
-    "gs_adam_step": (c_int, [c_int, P, P, P, P, P, P, c_double, c_double, c_double, c_longlong, P]),
+    "gs_adam_step": (c_int, [c_int, P, P, P, P, P, P, c_double, c_double, c_double, c_longlong,
+                             P, P, P]),
     "gs_sharded_adam_step": (c_int, [P, P, P, c_int, P, P, c_double, c_double, c_double,
-                                     c_longlong, c_float, P]),
+                                     c_longlong, c_float, P, P, P]),
     "gs_adc_workspace_size": (c_size_t, [c_int]),
     "gs_adc_plan": (c_int, [c_int, P, P, P, P, P, c_float, c_float, c_float, c_float, c_float,
                             c_int, c_int, P, c_size_t, P, P, P]),

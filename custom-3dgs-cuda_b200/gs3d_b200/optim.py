@@ -6,7 +6,10 @@ that layout, so one `gs_adam_step` launch updates every group: parameters, gradi
 moments are read and written once. It keeps torch's optimizer surface where the reference's
 trainer touches it: `param_groups` (one per parameter, with "lr" and "name", so learning-rate
 schedules work unchanged), `state[p]` with "step", "exp_avg" and "exp_avg_sq" (views into the
-flat moment buffers), `step()` and `zero_grad()`.
+flat moment buffers), `step()` and `zero_grad()`. A group may also hold "clamp": (lo, hi) (None
+or +-inf for an open side); the step then clamps that parameter in the same pass, as the
+reference trainer clamps opacity logits and log-scales after `optimizer.step()`
+(scripts/train.py:171-178).
 """
 
 from __future__ import annotations
@@ -16,6 +19,8 @@ import ctypes
 import torch
 
 from custom_rasterizer_cuda import _lib
+
+from .clamps import clamp_arrays
 
 
 class FlatAdam:
@@ -52,6 +57,7 @@ class FlatAdam:
         self.n_steps = 0
         self._sizes = (ctypes.c_longlong * len(sizes))(*sizes)
 
+
     def step(self) -> None:
         self.n_steps += 1
         k = len(self.params)
@@ -62,7 +68,7 @@ class FlatAdam:
             _lib.check(_lib.lib.gs_adam_step(
                 k, ptrs, self._sizes, lrs, self.flat_grad.data_ptr(), self.exp_avg.data_ptr(),
                 self.exp_avg_sq.data_ptr(), self.betas[0], self.betas[1], self.eps, self.n_steps,
-                torch.cuda.current_stream(dev).cuda_stream))
+                *clamp_arrays(self.param_groups), torch.cuda.current_stream(dev).cuda_stream))
         for p in self.params:
             self.state[p]["step"] = self.n_steps
 

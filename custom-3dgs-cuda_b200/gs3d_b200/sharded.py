@@ -25,6 +25,8 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from .clamps import clamp_arrays
+
 
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
@@ -206,7 +208,8 @@ class ShardedStep:
             self._lib.check(self._lib.lib.gs_sharded_adam_step(
                 ctypes.addressof(self.desc), self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(),
                 k, self._sizes, lrs, self.betas[0], self.betas[1], self.eps, self.n_steps,
-                1.0 / self.batch, torch.cuda.current_stream(self.device).cuda_stream))
+                1.0 / self.batch, *clamp_arrays(self.param_groups),
+                torch.cuda.current_stream(self.device).cuda_stream))
 
     def zero_grad(self, set_to_none: bool = False) -> None:
         self.bucket.zero_()

@@ -193,7 +193,8 @@ class Trainer:
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
                  fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct",
-                 view_streams: int = 6, tight_bins: bool = True):
+                 view_streams: int = 6, tight_bins: bool = True,
+                 param_clamps: dict | None = None):
         from gaussian_splatting.scene.gaussian import gaussian
 
         self.device = device
@@ -234,6 +235,12 @@ class Trainer:
             groups = [{"params": [getattr(g, n)], "lr": LEARNING_RATES[n], "name": n}
                       for n in PARAM_NAMES]
             self.opt = torch.optim.Adam(groups, lr=0.0, eps=1e-15)
+        # optional clamps after each update, by attribute name (gs3d_b200.clamps); the fused
+        # optimizers apply them in their own pass
+        self.param_clamps = dict(param_clamps or {})
+        for grp in self.opt.param_groups:
+            if grp["name"] in self.param_clamps:
+                grp["clamp"] = self.param_clamps[grp["name"]]
         self.fused_loss = fused_loss and device.type == "cuda"
         if mode not in ("direct", "autograd"):
             raise ValueError(f"unknown trainer mode {mode!r}")
@@ -259,6 +266,12 @@ class Trainer:
         if self.sharded is None:
             reduce_step(self.fg, len(self.views), self.world, self.group)
         self.opt.step()
+        if isinstance(self.opt, torch.optim.Optimizer):  # torch's Adam: clamps as torch ops
+            with torch.no_grad():
+                for grp in self.opt.param_groups:
+                    lo, hi = grp.get("clamp") or (None, None)
+                    if lo is not None or hi is not None:
+                        grp["params"][0].clamp_(lo, hi)
 
     def step(self, targets=None, before_view=None) -> torch.Tensor:
         if self.mode == "direct":

@@ -222,13 +222,17 @@ GS_API int gs_l1_ssim_backward(int H, int W, const float* img, const float* targ
  * and learning rate lrs[k] (host arrays); its gradients and moments are the slice starting at
  * sizes[0] + ... + sizes[k-1] of the flat device buffers grad, exp_avg and exp_avg_sq. `step` is
  * the 1-based step count used for bias correction; 1 - beta1, 1 - beta2 and the bias corrections
- * are formed in double on the host, as torch forms them from Python floats. No counterpart in the reference's
- * extension (its trainer calls torch's optimizer).
+ * are formed in double on the host, as torch forms them from Python floats. clamp_min /
+ * clamp_max (host arrays of n_groups floats, or NULL; -inf / +inf leave a side open): each
+ * group's updated parameters become min(max(p, clamp_min[k]), clamp_max[k]) in the same pass,
+ * the clamps the reference trainer applies right after optimizer.step() to the opacity logits
+ * and log-scales (scripts/train.py:171-178). No counterpart in the reference's extension (its
+ * trainer calls torch's optimizer).
  */
 GS_API int gs_adam_step(int n_groups, float* const* params, const long long* sizes,
                         const float* lrs, const float* grad, float* exp_avg, float* exp_avg_sq,
                         double beta1, double beta2, double eps, long long step,
-                        void* stream);
+                        const float* clamp_min, const float* clamp_max, void* stream);
 
 /*
  * The multi-GPU optimizer step of the view-parallel training step (no counterpart in the
@@ -243,6 +247,7 @@ GS_API int gs_adam_step(int n_groups, float* const* params, const long long* siz
  * scaled by grad_scale), SUM-reduced statistics at [stats_offset, stats_offset + n_stats), and
  * elements [r * max_shard, ...) of the MAX-reduced statistic (n_max non-negative floats).
  * exp_avg / exp_avg_sq hold this rank's shard of the Adam moments (shard floats each).
+ * clamp_min / clamp_max: per-group clamps of the updated parameters, as in gs_adam_step.
  * signal_pads is a device array of each rank's signal pad (signal_slots zeroed uint32 words);
  * barrier waits are bounded and a timeout sets a device error bit (gs_device_error_bits).
  */
@@ -269,7 +274,8 @@ typedef struct gs_shard_buffers {
 GS_API int gs_sharded_adam_step(const gs_shard_buffers* buffers, float* exp_avg,
                                 float* exp_avg_sq, int n_groups, const long long* group_sizes,
                                 const float* lrs, double beta1, double beta2, double eps,
-                                long long step, float grad_scale, void* stream);
+                                long long step, float grad_scale, const float* clamp_min,
+                                const float* clamp_max, void* stream);
 
 /*
  * Adaptive density control (the reference trainer's clone / split / prune / opacity reset,

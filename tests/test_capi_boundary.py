@@ -111,13 +111,14 @@ def test_training_entry_points_reject_bad_arguments_before_cuda():
     lrs = (ctypes.c_float * 1)(1e-3)
     ptrs = (ctypes.c_void_p * 1)(16)
     # more than 8 groups, a zero step, a beta outside [0, 1)
-    assert L.gs_adam_step(9, ptrs, sizes, lrs, 16, 16, 16, 0.9, 0.999, 1e-15, 1, None) == \
+    assert L.gs_adam_step(9, ptrs, sizes, lrs, 16, 16, 16, 0.9, 0.999, 1e-15, 1, None, None, None) == \
         _lib.GS_ERR_INVALID_ARG
-    assert L.gs_adam_step(1, ptrs, sizes, lrs, 16, 16, 16, 0.9, 0.999, 1e-15, 0, None) == \
+    assert L.gs_adam_step(1, ptrs, sizes, lrs, 16, 16, 16, 0.9, 0.999, 1e-15, 0, None, None, None) == \
         _lib.GS_ERR_INVALID_ARG
-    assert L.gs_adam_step(1, ptrs, sizes, lrs, 16, 16, 16, 1.0, 0.999, 1e-15, 1, None) == \
+    assert L.gs_adam_step(1, ptrs, sizes, lrs, 16, 16, 16, 1.0, 0.999, 1e-15, 1, None, None, None) == \
         _lib.GS_ERR_INVALID_ARG
-    assert L.gs_adam_step(0, None, None, None, None, None, None, 0.9, 0.999, 1e-15, 1, None) == 0
+    assert L.gs_adam_step(0, None, None, None, None, None, None, 0.9, 0.999, 1e-15, 1, None,
+                          None, None) == 0
 
     import sys
 
@@ -125,14 +126,19 @@ def test_training_entry_points_reject_bad_arguments_before_cuda():
     from gs3d_b200.sharded import ShardBuffers
 
     assert L.gs_sharded_adam_step(None, None, None, 1, sizes, lrs, 0.9, 0.999, 1e-15, 1, 1.0,
-                                  None) == _lib.GS_ERR_INVALID_ARG
+                                  None, None, None) == _lib.GS_ERR_INVALID_ARG
     d = ShardBuffers(world=2, rank=2, shard=8)  # rank out of range
     assert L.gs_sharded_adam_step(ctypes.addressof(d), 16, 16, 1, sizes, lrs, 0.9, 0.999, 1e-15,
-                                  1, 1.0, None) == _lib.GS_ERR_INVALID_ARG
+                                  1, 1.0, None, None, None) == _lib.GS_ERR_INVALID_ARG
     assert b"rank" in L.gs_last_error()
     d = ShardBuffers(world=2, rank=0, shard=6)  # shard not a multiple of 4
     assert L.gs_sharded_adam_step(ctypes.addressof(d), 16, 16, 1, sizes, lrs, 0.9, 0.999, 1e-15,
-                                  1, 1.0, None) == _lib.GS_ERR_INVALID_ARG
+                                  1, 1.0, None, None, None) == _lib.GS_ERR_INVALID_ARG
+    # a clamp whose lower bound is above its upper bound
+    lo, hi = (ctypes.c_float * 1)(1.0), (ctypes.c_float * 1)(0.0)
+    assert L.gs_adam_step(1, ptrs, sizes, lrs, 16, 16, 16, 0.9, 0.999, 1e-15, 1, lo, hi,
+                          None) == _lib.GS_ERR_INVALID_ARG
+    assert b"clamp" in L.gs_last_error()
     # unknown render flag
     assert L.gs_render_forward(1, 16, 16, *([16] * 9), 1.0, 1.0, 8.0, 8.0, 256, 1 << 20, 16,
                                *([256] * 6), None, None, 0x80, None) == _lib.GS_ERR_INVALID_ARG

@@ -1,7 +1,8 @@
 """The multi-GPU training step (gs_sharded_adam_step through gs3d_b200.sharded): two ranks, one
 GPU each, each rendering half of a 4-view batch, against the single-GPU trainer on the whole
 batch. Both data paths are run: NVLink multicast (multimem reductions and broadcasts in the
-switch) and plain peer loads / stores. Skipped on machines with fewer than two GPUs."""
+switch) and plain peer loads / stores. Both trainers clamp the opacity logits and log-scales
+after each update (in the fused kernels). Skipped on machines with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -17,6 +18,8 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 STEPS = 2
+# clamps after each update (the reference trainer's kind, tighter so that they bind)
+CLAMPS = {"alpha": (-1.0, 1.0), "s": (None, -4.0)}
 
 
 def _free_port() -> int:
@@ -58,7 +61,8 @@ def _worker(rank: int, world: int, port: int, peer: bool, q) -> None:
         from gs3d_b200.train_step import Trainer
 
         sc, views, targets = _setup()
-        tr = Trainer(sc, views, [t.to(dev) for t in targets], dev, rank, world)
+        tr = Trainer(sc, views, [t.to(dev) for t in targets], dev, rank, world,
+                     param_clamps=CLAMPS)
         for _ in range(STEPS):
             tr.step()
         torch.cuda.synchronize(dev)
@@ -99,7 +103,7 @@ def test_sharded_step_matches_single_gpu(peer):
 
     dev = torch.device("cuda", 0)
     sc, views, targets = _setup()
-    ref_tr = Trainer(sc, views, [t.to(dev) for t in targets], dev)
+    ref_tr = Trainer(sc, views, [t.to(dev) for t in targets], dev, param_clamps=CLAMPS)
     init = [p.detach().cpu().clone() for p in ref_tr.params]
     for _ in range(STEPS):
         ref_tr.step()
@@ -110,6 +114,9 @@ def test_sharded_step_matches_single_gpu(peer):
     for a, b in zip(p0, p1):  # one writer per element: the ranks hold identical parameters
         assert torch.equal(a, b)
     for name, mine, theirs, start in zip(PARAM_NAMES, p0, ref[0], init):
+        if name in CLAMPS:
+            lo, hi = CLAMPS[name]
+            assert float(mine.max()) <= hi and (lo is None or float(mine.min()) >= lo), name
         d_mine = (mine - start).numpy().ravel()
         d_ref = (theirs - start).numpy().ravel()
         assert np.abs(d_ref).max() > 0, name

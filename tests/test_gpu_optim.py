@@ -49,6 +49,48 @@ def test_flat_adam_matches_torch_adam(cuda_device, sizes):
         assert st["step"] == 6
 
 
+def test_flat_adam_clamps_like_torch_clamp_after_step(cuda_device):
+    """A group's "clamp" bounds give the same parameters as torch Adam followed by clamp_ (the
+    reference trainer's opacity / log-scale clamps), unclamped groups are untouched."""
+    from gs3d_b200.optim import FlatAdam
+
+    g = torch.Generator("cpu").manual_seed(3)
+    sizes, lrs = (5000, 3000, 700), [5e-2, 5e-3, 1e-3]
+    clamps = [(-0.5, 0.5), (None, 0.25), None]
+    init = [torch.randn(k, generator=g) for k in sizes]
+    mine = [t.clone().to(cuda_device) for t in init]
+    ref = [t.clone().to(cuda_device).requires_grad_(True) for t in init]
+    flat = torch.zeros(sum(sizes), device=cuda_device)
+    off = 0
+    for p, k in zip(mine, sizes):
+        p.grad = flat[off:off + k]
+        off += k
+    opt = FlatAdam(mine, lrs, ["alpha", "s", "q"], flat, eps=1e-15)
+    for grp, c in zip(opt.param_groups, clamps):
+        if c is not None:
+            grp["clamp"] = c
+    torch_opt = torch.optim.Adam([{"params": [p], "lr": lr} for p, lr in zip(ref, lrs)],
+                                 lr=0.0, eps=1e-15)
+    for _ in range(4):
+        grads = [torch.randn(k, generator=g).to(cuda_device) for k in sizes]
+        flat.copy_(torch.cat(grads))
+        for p, gr in zip(ref, grads):
+            p.grad = gr.clone()
+        opt.step()
+        torch_opt.step()
+        with torch.no_grad():
+            for p, c in zip(ref, clamps):
+                if c is not None:
+                    p.clamp_(*c)
+    torch.cuda.synchronize()
+    for p, r, c in zip(mine, ref, clamps):
+        torch.testing.assert_close(p, r.detach(), rtol=1e-6, atol=1e-6)
+        if c is not None:
+            lo = -float("inf") if c[0] is None else c[0]
+            assert float(p.min()) >= lo and float(p.max()) <= c[1]
+            assert bool((p == c[1]).any())  # the bound was reached
+
+
 def test_flat_adam_rejects_grads_outside_the_buffer(cuda_device):
     from gs3d_b200.optim import FlatAdam
 
