@@ -54,10 +54,11 @@ def _reduce_worker(rank: int, world: int, port: int, batch: int, q) -> None:
         dist.destroy_process_group()
 
 
-def _run_ranks(target, world, extra, attempts=2):
+def _run_ranks(target, world, extra, attempts=3):
     """Spawns `world` ranks of `target(rank, world, port, *extra, queue)` and collects one
-    queue item per rank; a second attempt with a fresh port covers a port another process took
-    between _free_port() and the rendezvous."""
+    queue item per rank; further attempts with a fresh port cover a port another process took
+    between _free_port() and the rendezvous (a rank that fails there can also break the result
+    queue's pipe)."""
     import queue as queue_mod
 
     ctx = mp.get_context("spawn")
@@ -70,7 +71,7 @@ def _run_ranks(target, world, extra, attempts=2):
             p.start()
         try:
             results = [q.get(timeout=120) for _ in range(world)]
-        except queue_mod.Empty:
+        except (queue_mod.Empty, OSError, EOFError):
             results = None
         for p in procs:
             p.join(timeout=60)
