@@ -387,7 +387,7 @@ def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n:
     ms = stage_ms[name]
     mean_replayed = statistics.mean(stats["replayed_pairs"])
     mean_pairs = statistics.mean(stats["pairs"])
-    # algorithmic bytes per unit
+    # algorithmic bytes per launch: per-unit bytes of each kernel times the units it processes
     hbm_bytes = {
         "preprocess": 236 * n + 56 * n,             # parameters in; rects + records out
         "depth_sort": 4 * 16 * n,                   # 4 passes over (key, id) of N_v <= N

@@ -20,7 +20,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-DEFAULT_REFERENCE = Path("/root/reference")
+# a checkout of the reference next to this repository
+DEFAULT_REFERENCE = HERE.parents[1] / "reference"
 
 
 def build(reference: Path = DEFAULT_REFERENCE, verbose: bool = False) -> Path | None:
