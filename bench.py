@@ -378,6 +378,10 @@ NCU_DRAM_BYTES = {
     "preprocess": 284.1e6, "duplicate": 12.2e6, "blend_forward": 67.5e6,
     "blend_backward": 135.9e6, "gaussian_backward": 497.9e6,
 }
+# warp instructions (smsp__inst_executed.sum) per launch of the blend kernels from the same
+# capture: the blends are bound by instruction issue (one warp instruction per cycle on each
+# of the 4 x 148 schedulers), not by FP32 FMA throughput
+NCU_WARP_INST = {"blend_forward": 289.6e6, "blend_backward": 567.2e6}
 
 
 def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int) -> dict:
@@ -405,13 +409,21 @@ def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n:
     fp32_peak = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6 / 1e12  # TFLOP/s
     flops_per_pair = 40.0 if name == "blend_backward" else 14.0
     achieved = flops_per_pair * mean_replayed / (ms * 1e-3) / 1e12
-    return {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": fp32_peak,
-            "unit": "TFLOP/s", "frac": achieved / fp32_peak,
-            "traffic": NCU_DRAM_BYTES.get(name), "traffic_unit": "bytes per launch (ncu)",
-            "peak_source": "derived: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz",
-            "ms_per_launch": ms,
-            "unit_of_work": f"{flops_per_pair:.0f} FLOP per replayed (pixel, Gaussian) pair, "
-                            f"{mean_replayed:.3g} per view"}
+    entry = {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": fp32_peak,
+             "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+             "traffic": NCU_DRAM_BYTES.get(name), "traffic_unit": "bytes per launch (ncu)",
+             "peak_source": "derived: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz",
+             "ms_per_launch": ms,
+             "unit_of_work": f"{flops_per_pair:.0f} FLOP per replayed (pixel, Gaussian) pair, "
+                             f"{mean_replayed:.3g} per view"}
+    if name in NCU_WARP_INST:
+        issue_peak = 148 * 4 * pk["sm_max_mhz"] * 1e6 / 1e9  # G warp instructions/s
+        issued = NCU_WARP_INST[name] / (ms * 1e-3) / 1e9
+        entry["issue"] = {"achieved": issued, "peak": issue_peak, "unit": "G warp inst/s",
+                          "frac": issued / issue_peak,
+                          "warp_inst_per_launch": NCU_WARP_INST[name],
+                          "source": "ncu smsp__inst_executed.sum of the same kernel variant"}
+    return entry
 
 
 # ---- CPU baseline (the oracle) ----------------------------------------------------------------
