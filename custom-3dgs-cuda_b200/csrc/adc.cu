@@ -14,7 +14,8 @@
 // counts into block offsets and totals, which reach the host through a pinned copy.
 //
 // gs_adc_apply writes the result in the reference's order, [kept originals][kept clones]
-// [kept first children][kept second children], each in index order: parameters copied (a
+// [kept first children][kept second children], each in index order (each warp copies its 32
+// Gaussians' rows group by group with coalesced loads): parameters copied (a
 // child's mean is R(q) (z * exp(s)) + mu with the caller's unit normals z, its log-scales
 // log(exp(s) / 1.6)), Adam moments copied for originals and zero for new Gaussians, and
 // with the opacity reset alpha = min(alpha, logit(0.01)) and zero opacity moments.
@@ -30,7 +31,6 @@ constexpr int kAdcThreads = 256;
 constexpr int kAdcScanThreads = 1024;
 constexpr int kAdcGroups = 6;
 constexpr int kAdcCats = 5;  // kept originals, kept clones, split, kept children, clones
-__constant__ int c_adc_dims[kAdcGroups] = {3, 4, 3, 1, 3, 45};  // mu, q, s, alpha, A, k_j
 
 enum : unsigned char {
   kAdcClone = 1, kAdcSplit = 2, kAdcKeepOrig = 4, kAdcKeepClone = 8, kAdcKeepChild = 16,
@@ -169,26 +169,47 @@ __device__ __forceinline__ unsigned block_rank(bool pred, unsigned* s_warp, unsi
   return before + __popc(ballot & ((1u << lane) - 1u));
 }
 
-__device__ __forceinline__ void copy_row(const AdcApply& a, int k, int src, long long dst,
-                                         bool moments_from_src, bool reset) {
-  const int d = c_adc_dims[k];
-  const float* in = a.in[k] + (size_t)src * d;
-  float* out = a.out[k] + (size_t)dst * d;
-  for (int j = 0; j < d; ++j) {
-    float v = in[j];
-    if (k == 3 && reset) v = fminf(v, a.opacity_cap);
-    out[j] = v;
+// Warp-cooperative row copy of one parameter group (D floats per row): the warp's 32
+// Gaussians' rows are contiguous in the source, so the lanes walk those 32 D floats in order
+// (coalesced loads); each float goes to row dst_row of its owner lane (taken by shuffle), or
+// nowhere when that is negative. `zero` writes zeros instead (new Gaussians' Adam moments),
+// `cap` applies the opacity reset min(v, cap_v).
+template <int D>
+__device__ __forceinline__ void warp_copy_rows(const float* __restrict__ src,
+                                               float* __restrict__ dst, long long row0,
+                                               long long dst_row, bool zero, bool cap,
+                                               float cap_v) {
+  const int lane = threadIdx.x & 31;
+  const float* s = src + row0 * D;
+#pragma unroll 4
+  for (int e = lane; e < 32 * D; e += 32) {
+    const int r = e / D, c = e - r * D;
+    const long long dr = __shfl_sync(0xffffffffu, dst_row, r);
+    if (dr >= 0) {
+      float v = zero ? 0.0f : s[e];
+      if (cap) v = fminf(v, cap_v);
+      dst[dr * D + c] = v;
+    }
   }
-  const bool zero = !moments_from_src || (k == 3 && reset);
-  if (a.m_out[k]) {
-    float* mo = a.m_out[k] + (size_t)dst * d;
-    const float* mi = a.m_in[k] + (size_t)src * d;
-    for (int j = 0; j < d; ++j) mo[j] = zero ? 0.0f : mi[j];
-  }
-  if (a.v_out[k]) {
-    float* vo = a.v_out[k] + (size_t)dst * d;
-    const float* vi = a.v_in[k] + (size_t)src * d;
-    for (int j = 0; j < d; ++j) vo[j] = zero ? 0.0f : vi[j];
+}
+
+// Group k of the warp's rows to up to four destinations (kept original, kept clone, the two
+// kept children), with the moments; the children's means and log-scales are written per lane
+// afterwards (do_params false for those groups).
+template <int D>
+__device__ __forceinline__ void warp_copy_group(const AdcApply& a, int k, long long row0,
+                                                const long long (&dst)[4], bool do_params,
+                                                bool reset) {
+  const bool cap = k == 3 && reset;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    if (!__any_sync(0xffffffffu, dst[t] >= 0)) continue;
+    if (do_params || t < 2) warp_copy_rows<D>(a.in[k], a.out[k], row0, dst[t], false, cap,
+                                              a.opacity_cap);
+    // moments: copied for originals (zero under the opacity reset), zero for new Gaussians
+    const bool zero = t > 0 || cap;
+    if (a.m_out[k]) warp_copy_rows<D>(a.m_in[k], a.m_out[k], row0, dst[t], zero, false, 0.f);
+    if (a.v_out[k]) warp_copy_rows<D>(a.v_in[k], a.v_out[k], row0, dst[t], zero, false, 0.f);
   }
 }
 
@@ -202,41 +223,45 @@ __global__ void __launch_bounds__(kAdcThreads) adc_apply_kernel(AdcApply a) {
   const unsigned r_clone = block_rank(f & kAdcKeepClone, s_warp, &tot);
   const unsigned r_split = block_rank(f & kAdcSplit, s_warp, &tot);
   const unsigned r_child = block_rank(f & kAdcKeepChild, s_warp, &tot);
-  if (i >= a.N) return;
   const bool reset = a.reset_opacity != 0;
-  if (f & kAdcKeepOrig) {
-    const long long dst = (long long)off[0] + r_orig;
-    for (int k = 0; k < kAdcGroups; ++k) copy_row(a, k, i, dst, true, reset);
-  }
-  if (f & kAdcKeepClone) {
-    const long long dst = a.n_orig + (long long)off[1] + r_clone;
-    for (int k = 0; k < kAdcGroups; ++k) copy_row(a, k, i, dst, false, reset);
-  }
+  // destination rows of this lane's Gaussian: kept original, kept clone, first and second child
+  long long dst[4] = {-1, -1, -1, -1};
+  if (f & kAdcKeepOrig) dst[0] = (long long)off[0] + r_orig;
+  if (f & kAdcKeepClone) dst[1] = a.n_orig + (long long)off[1] + r_clone;
   if (f & kAdcKeepChild) {
-    const long long row = (long long)off[2] + r_split;  // this Gaussian's rank among splits
-    const long long ci = (long long)off[3] + r_child;
-    const float* mu = a.in[0] + 3 * (size_t)i;
-    const float* q = a.in[1] + 4 * (size_t)i;
-    const float* s = a.in[2] + 3 * (size_t)i;
-    const float nq = sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
-    const float inv = 1.0f / fmaxf(nq, 1e-12f);
-    const float w = q[0] * inv, x = q[1] * inv, y = q[2] * inv, z = q[3] * inv;
-    const float R[3][3] = {
-        {1.0f - 2.0f * (y * y + z * z), 2.0f * (x * y - w * z), 2.0f * (x * z + w * y)},
-        {2.0f * (x * y + w * z), 1.0f - 2.0f * (x * x + z * z), 2.0f * (y * z - w * x)},
-        {2.0f * (x * z - w * y), 2.0f * (y * z + w * x), 1.0f - 2.0f * (x * x + y * y)}};
-    const float e[3] = {expf(s[0]), expf(s[1]), expf(s[2])};
-    for (int copy = 0; copy < 2; ++copy) {
-      const long long dst = a.n_orig + a.n_clone + copy * a.n_child + ci;
-      const float* zr = a.z + 3 * (size_t)(copy * a.n_split + row);
-      const float smp[3] = {0.0f + zr[0] * e[0], 0.0f + zr[1] * e[1], 0.0f + zr[2] * e[2]};
-      for (int k = 0; k < kAdcGroups; ++k) copy_row(a, k, i, dst, false, reset);
-      float* mo = a.out[0] + 3 * (size_t)dst;
-      float* so = a.out[2] + 3 * (size_t)dst;
-      for (int c = 0; c < 3; ++c) {
-        mo[c] = (R[c][0] * smp[0] + R[c][1] * smp[1] + R[c][2] * smp[2]) + mu[c];
-        so[c] = logf(e[c] / 1.6f);
-      }
+    dst[2] = a.n_orig + a.n_clone + (long long)off[3] + r_child;
+    dst[3] = dst[2] + a.n_child;
+  }
+  const long long row0 = (long long)blockIdx.x * kAdcThreads + (threadIdx.x & ~31);
+  warp_copy_group<3>(a, 0, row0, dst, false, reset);  // mu: children computed below
+  warp_copy_group<4>(a, 1, row0, dst, true, reset);
+  warp_copy_group<3>(a, 2, row0, dst, false, reset);  // s: children computed below
+  warp_copy_group<1>(a, 3, row0, dst, true, reset);
+  warp_copy_group<3>(a, 4, row0, dst, true, reset);
+  warp_copy_group<45>(a, 5, row0, dst, true, reset);
+  if (i >= a.N || !(f & kAdcKeepChild)) return;
+  // the two children's means R(q)(z * exp(s)) + mu and log-scales log(exp(s) / 1.6)
+  const long long row = (long long)off[2] + r_split;  // this Gaussian's rank among splits
+  const float* mu = a.in[0] + 3 * (size_t)i;
+  const float* q = a.in[1] + 4 * (size_t)i;
+  const float* s = a.in[2] + 3 * (size_t)i;
+  const float nq = sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
+  const float inv = 1.0f / fmaxf(nq, 1e-12f);
+  const float w = q[0] * inv, x = q[1] * inv, y = q[2] * inv, z = q[3] * inv;
+  const float R[3][3] = {
+      {1.0f - 2.0f * (y * y + z * z), 2.0f * (x * y - w * z), 2.0f * (x * z + w * y)},
+      {2.0f * (x * y + w * z), 1.0f - 2.0f * (x * x + z * z), 2.0f * (y * z - w * x)},
+      {2.0f * (x * z - w * y), 2.0f * (y * z + w * x), 1.0f - 2.0f * (x * x + y * y)}};
+  const float e[3] = {expf(s[0]), expf(s[1]), expf(s[2])};
+  for (int copy = 0; copy < 2; ++copy) {
+    const long long d = dst[2 + copy];
+    const float* zr = a.z + 3 * (size_t)(copy * a.n_split + row);
+    const float smp[3] = {0.0f + zr[0] * e[0], 0.0f + zr[1] * e[1], 0.0f + zr[2] * e[2]};
+    float* mo = a.out[0] + 3 * (size_t)d;
+    float* so = a.out[2] + 3 * (size_t)d;
+    for (int c = 0; c < 3; ++c) {
+      mo[c] = (R[c][0] * smp[0] + R[c][1] * smp[1] + R[c][2] * smp[2]) + mu[c];
+      so[c] = logf(e[c] / 1.6f);
     }
   }
 }
