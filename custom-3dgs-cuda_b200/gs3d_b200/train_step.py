@@ -17,7 +17,6 @@ gloo in the CPU tests).
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
