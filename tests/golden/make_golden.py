@@ -19,7 +19,8 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
-sys.path[:0] = [str(ROOT), str(ROOT / "custom-3dgs-cuda_b200"), str(ROOT / "oracle" / "_ref")]
+sys.path[:0] = [str(ROOT), str(ROOT / "custom-3dgs-cuda_b200"), str(ROOT / "oracle" / "_ref" / "ref_raster"),
+                str(ROOT / "oracle" / "_ref" / "ref_full")]
 
 from gs3d_b200 import scenes  # noqa: E402
 from oracle import oracle as O  # noqa: E402

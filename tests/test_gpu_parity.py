@@ -179,7 +179,7 @@ def test_matches_reference_golden(crc, cuda_device, path):
 def _ref_module():
     import sys
 
-    p = str(ROOT / "oracle" / "_ref")
+    p = str(ROOT / "oracle" / "_ref" / "ref_raster")
     if p not in sys.path:
         sys.path.insert(0, p)
     try:
