@@ -39,32 +39,38 @@ __device__ __forceinline__ float3 world_to_camera(const Camera& cam, float x, fl
 
 constexpr float kNearCull = 0.2f;  // csrc/forward/projection.cu:47
 
-// Rotation matrix (row-major) of the normalised quaternion (w,x,y,z). Normalisation divides
-// by the Euclidean length, (w^2 + x^2) + (y^2 + z^2), and a zero quaternion maps to the
-// identity rotation; the matrix entries are the standard unit-quaternion rotation.
+// Rotation matrix (row-major) of the normalised quaternion (w,x,y,z): the reference's
+// glm::toMat3(glm::normalize(quat(w,x,y,z))) (csrc/forward/projection.cu:64-65). Normalisation
+// multiplies by 1 / sqrt((w^2 + x^2) + (y^2 + z^2)) and maps a zero quaternion to the identity;
+// the entries are the standard unit-quaternion rotation. Every rounding step is written with an
+// explicit intrinsic, in the order the reference's build evaluates it (each sum of two products
+// fuses its first product; the (0,0) entry adds the two rounded squares), so the compiler
+// cannot re-associate or re-fuse them differently in different kernels: the rotation, and with
+// it the 2D covariance, is bit-identical to the reference's.
 __device__ __forceinline__ void quat_to_rotation(float qw, float qx, float qy, float qz,
                                                  float* Rq, float4& qn) {
-  float len = sqrtf((qw * qw + qx * qx) + (qy * qy + qz * qz));
+  const float dot = __fadd_rn(__fmaf_rn(qw, qw, __fmul_rn(qx, qx)),
+                              __fmaf_rn(qy, qy, __fmul_rn(qz, qz)));
+  const float len = sqrtf(dot);
   float w, x, y, z;
   if (len <= 0.0f) {
     w = 1.0f; x = 0.0f; y = 0.0f; z = 0.0f;
   } else {
-    float inv = 1.0f / len;
-    w = qw * inv; x = qx * inv; y = qy * inv; z = qz * inv;
+    const float inv = __fdiv_rn(1.0f, len);
+    w = __fmul_rn(qw, inv); x = __fmul_rn(qx, inv); y = __fmul_rn(qy, inv); z = __fmul_rn(qz, inv);
   }
   qn = make_float4(w, x, y, z);
-  float xx = x * x, yy = y * y, zz = z * z;
-  float xz = x * z, xy = x * y, yz = y * z;
-  float wx = w * x, wy = w * y, wz = w * z;
-  Rq[0] = 1.0f - 2.0f * (yy + zz);
-  Rq[3] = 2.0f * (xy + wz);
-  Rq[6] = 2.0f * (xz - wy);
-  Rq[1] = 2.0f * (xy - wz);
-  Rq[4] = 1.0f - 2.0f * (xx + zz);
-  Rq[7] = 2.0f * (yz + wx);
-  Rq[2] = 2.0f * (xz + wy);
-  Rq[5] = 2.0f * (yz - wx);
-  Rq[8] = 1.0f - 2.0f * (xx + yy);
+  const float yy = __fmul_rn(y, y), zz = __fmul_rn(z, z);
+  const float wx = __fmul_rn(w, x), wy = __fmul_rn(w, y), wz = __fmul_rn(w, z);
+  Rq[0] = __fmaf_rn(-2.0f, __fadd_rn(yy, zz), 1.0f);
+  Rq[3] = 2.0f * __fmaf_rn(x, y, wz);
+  Rq[6] = 2.0f * __fmaf_rn(x, z, -wy);
+  Rq[1] = 2.0f * __fmaf_rn(x, y, -wz);
+  Rq[4] = __fmaf_rn(-2.0f, __fmaf_rn(x, x, zz), 1.0f);
+  Rq[7] = 2.0f * __fmaf_rn(y, z, wx);
+  Rq[2] = 2.0f * __fmaf_rn(x, z, wy);
+  Rq[5] = 2.0f * __fmaf_rn(y, z, -wx);
+  Rq[8] = __fmaf_rn(-2.0f, __fmaf_rn(x, x, yy), 1.0f);
 }
 
 // C = A * B for row-major 3x3 matrices, each entry summed over k = 0, 1, 2 in order.

@@ -68,9 +68,11 @@ static void quat_rot(const float* q, float* Rq, float* qn) {
     w *= inv; x *= inv; y *= inv; z *= inv;
   }
   qn[0] = w; qn[1] = x; qn[2] = y; qn[3] = z;
-  /* glm mat3_cast: products formed once, sums of two products contracted */
+  /* glm mat3_cast as the reference's build evaluates it (measured against the ref+shim build
+   * on a B200): sums of two products fuse the first product, except the (0,0) entry, which
+   * adds the two rounded squares */
   float yy = y * y, zz = z * z, wx = w * x, wy = w * y, wz = w * z;
-  Rq[0] = fmaf(-2.0f, fmaf(y, y, zz), 1.0f);
+  Rq[0] = fmaf(-2.0f, yy + zz, 1.0f);
   Rq[3] = 2.0f * fmaf(x, y, wz);
   Rq[6] = 2.0f * fmaf(x, z, -wy);
   Rq[1] = 2.0f * fmaf(x, y, -wz);

@@ -1,12 +1,20 @@
-"""Generates the golden vectors tests/golden/ref_raster_*.npz on a CUDA machine.
+"""Generates the golden vectors tests/golden/ref_raster_*.npz and ref_gaussian_*.npz on a CUDA
+machine, from the REFERENCE's own kernels built by oracle/build_ref.py.
 
-Inputs (mean2d, cov2d, depths, colors, opacity) come from the CPU oracle's projection and SH
-of seeded scenes; the outputs come from the REFERENCE's own binning / blend kernels
-(csrc/forward/rasterize.cu, csrc/backward/rasterize_backward.cu, built unmodified into
-oracle/_ref by oracle/build_ref.py). The files pin the oracle (tests/test_oracle_kat.py) and
-the CUDA path (tests/test_gpu_parity.py) to the reference's behaviour.
+* ref_raster_*: inputs (mean2d, cov2d, depths, colors, opacity) come from the CPU oracle's
+  projection and SH of seeded scenes; the outputs come from the reference's binning / blend
+  kernels (csrc/forward/rasterize.cu, csrc/backward/rasterize_backward.cu, built unmodified,
+  module ref_raster).
+* ref_gaussian_*: the per-Gaussian stages -- `project`, `SH`, `backwards_SH`,
+  `backwards_projection` (csrc/forward/projection.cu, csrc/forward/SH.cu,
+  csrc/backward/delight_backward.cu, csrc/backward/projection_backward.cu) -- of the
+  reference's whole extension built against the GLM stand-in oracle/glm_shim (module ref_full,
+  "ref+shim"), on seeded Gaussians, cameras and upstream gradients stored in the file.
 
-Usage (GPU box): python tests/golden/make_golden.py [--out DIR]
+The files pin the oracle (tests/test_oracle_kat.py) and the CUDA path (tests/test_gpu_parity.py,
+tests/test_gpu_ref_shim.py) to the reference's behaviour.
+
+Usage (GPU box): python tests/golden/make_golden.py [--out DIR] [--only raster|gaussian]
 """
 
 from __future__ import annotations
@@ -68,15 +76,77 @@ def make(name, sc, view, ref, out_dir: Path, seed: int):
     print(f"{path.name}: N={sc.N} M={ids.numel()} {W}x{H}", flush=True)
 
 
+def gaussian_cases():
+    """(name, scene, view): 1,024 Gaussians each (small files), plus hand-made edge rows."""
+    sc0 = scenes.config0(0)
+    yield "config0", sub_scene(sc0, 0, 1024, edge_rows=True), sc0.views[0]
+    sc1 = scenes.config1(0)
+    yield "config1_1080", sub_scene(sc1, 5000, 1024), sc1.views[1]
+    behind = scenes.config0(2)
+    yield "partly_behind_camera", sub_scene(behind, 0, 1024), scenes.pinhole(
+        (0.0, 0.0, 0.5), 96, 64, 64.0)
+
+
+def sub_scene(sc, start, n, edge_rows=False):
+    p = [x[start:start + n].clone() for x in sc.params()]
+    if edge_rows:
+        # a zero quaternion (normalised to the identity), an unnormalised one, a quaternion with
+        # a negative real part, extreme log-scales, a Gaussian just in front of the near plane
+        # and one just behind it (camera at z = 4 looking down -z: depth = 4 - z)
+        mu, q, s = p[0], p[1], p[2]
+        q[0] = 0.0
+        q[1] = torch.tensor([3.0, -1.0, 0.5, 2.0])
+        q[2] = torch.tensor([-0.9, 0.1, 0.3, -0.2])
+        s[3] = torch.tensor([-12.0, -12.0, -12.0])
+        s[4] = torch.tensor([1.5, -9.0, 0.5])
+        mu[5] = torch.tensor([0.01, -0.02, 4.0 - 0.2001])
+        mu[6] = torch.tensor([0.01, -0.02, 4.0 - 0.2])
+    return scenes.Scene(sc.name, *p)
+
+
+def make_gaussian(name, sc, view, ref, out_dir: Path, seed: int):
+    dev = torch.device("cuda")
+    mu, q, s, _, A, kj = [x.to(dev).contiguous() for x in sc.params()]
+    R, t = view.R.to(dev).contiguous(), view.T.to(dev).contiguous()
+    cam = (-(R.T @ t)).contiguous()
+    N = sc.N
+    mean2d, cov2d, depths = ref.project(N, mu, q, s, R, t, view.fx, view.fy, view.cx, view.cy)
+    colors = ref.SH(N, cam, mu, A, kj)
+    g = torch.Generator("cpu").manual_seed(seed)
+    g_colors = torch.randn(N, 3, generator=g).to(dev)
+    g_mean2d = torch.randn(N, 2, generator=g).to(dev)
+    g_cov2d = (0.1 * torch.randn(N, 3, generator=g)).to(dev)
+    gA, gkj, gmu_sh = ref.backwards_SH(g_colors, mu, A, kj, cam)
+    gmu, gq, gs = ref.backwards_projection(g_mean2d, g_cov2d, mu, q, s, R, t, view.fx, view.fy,
+                                           view.cx, view.cy)
+    torch.cuda.synchronize()
+    cpu = lambda x: x.detach().cpu().numpy()  # noqa: E731
+    path = out_dir / f"ref_gaussian_{name}.npz"
+    np.savez_compressed(
+        path, mu=cpu(mu), q=cpu(q), s=cpu(s), A=cpu(A), k_j=cpu(kj), R=cpu(R), t=cpu(t),
+        cam=cpu(cam), intr=np.array([view.fx, view.fy, view.cx, view.cy], np.float32),
+        mean2d=cpu(mean2d), cov2d=cpu(cov2d), depths=cpu(depths), colors=cpu(colors),
+        g_colors=cpu(g_colors), g_mean2d=cpu(g_mean2d), g_cov2d=cpu(g_cov2d), g_A=cpu(gA),
+        g_k_j=cpu(gkj), g_mu_sh=cpu(gmu_sh), g_mu=cpu(gmu), g_q=cpu(gq), g_s=cpu(gs))
+    print(f"{path.name}: N={N} culled={int((depths == 0).sum())}", flush=True)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--out", type=Path, default=Path(__file__).resolve().parent)
+    ap.add_argument("--only", choices=("raster", "gaussian"), default=None)
     args = ap.parse_args()
-    import ref_raster as ref  # built by oracle/build_ref.py
-
     args.out.mkdir(parents=True, exist_ok=True)
-    for k, (name, sc, view) in enumerate(cases()):
-        make(name, sc, view, ref, args.out, seed=100 + k)
+    if args.only in (None, "raster"):
+        import ref_raster as ref  # built by oracle/build_ref.py
+
+        for k, (name, sc, view) in enumerate(cases()):
+            make(name, sc, view, ref, args.out, seed=100 + k)
+    if args.only in (None, "gaussian"):
+        import ref_full  # built by oracle/build_ref.py (ref+shim)
+
+        for k, (name, sc, view) in enumerate(gaussian_cases()):
+            make_gaussian(name, sc, view, ref_full, args.out, seed=200 + k)
     return 0
 
 
