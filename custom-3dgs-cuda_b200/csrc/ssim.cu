@@ -1,6 +1,13 @@
 // Fused photometric loss of the training step: L = (1 - l) * mean|x - y| + l * (1 - SSIM(x, y))
-// on [H, W, 3] images, SSIM with an 11x11 Gaussian window (sigma 1.5, zero padding,
-// C1 = 0.01^2, C2 = 0.03^2), averaged over pixels and channels.
+// on [H, W, 3] images, with the semantics of the reference's loss
+// (gaussian_splatting/utils/loss.py:8-33: torchmetrics'
+// structural_similarity_index_measure(preds = x, target = y, data_range = 1.0) on the images
+// clamped to [0, 1]): an 11x11 Gaussian window (sigma 1.5), C1 = 0.01^2, C2 = 0.03^2, variances
+// clamped at zero, and the SSIM map averaged over the channels and the (H - 10) x (W - 10)
+// interior positions. torchmetrics reflect-pads by 5 and then crops those 5 rows and columns
+// from the map, so every remaining window lies inside the image and the padding never reaches
+// the result: the interior map is what is computed here. The L1 term uses the unclamped
+// images and is averaged over all 3 H W values.
 //
 // Forward (one kernel + a one-block reduction): each CTA takes a 32x32 output tile and, one
 // channel at a time, stages that channel's x and y with a 5-pixel halo in shared memory, blurs
@@ -78,7 +85,11 @@ __device__ __forceinline__ void store_run(float* dst, const float (&v)[kSsimRun]
     d4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
 }
 
-// Derivative maps are planar: maps[(3 * kind + channel) * H * W + pixel], kind A, B, Cm.
+// Derivative maps are planar: maps[(3 * kind + channel) * H * W + pixel], kind A, B, Cm; they
+// are zero outside the interior (positions whose window leaves the image), so the backward's
+// blurs of them only gather from interior positions.
+__device__ __forceinline__ float clamp01(float v) { return fminf(fmaxf(v, 0.f), 1.f); }
+
 __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
     int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
     float* __restrict__ maps, double* __restrict__ partials) {
@@ -111,8 +122,8 @@ __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
             a[rr][u] = b[rr][u] = 0.f;
             if (row_ok && px < kSsimInW && gxx >= 0 && gxx < W) {
               const size_t o = ((size_t)gy * W + gxx) * 3 + c;
-              a[rr][u] = __ldg(img + o);
-              b[rr][u] = __ldg(ref + o);
+              a[rr][u] = clamp01(__ldg(img + o));
+              b[rr][u] = clamp01(__ldg(ref + o));
             }
           }
         }
@@ -171,23 +182,30 @@ __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
       for (int o = 0; o < kSsimRun; ++o) {
         const int r = rb * kSsimRun + o, gy = by + r;
         if (gx >= W || gy >= H) continue;
-        const float mx = m[0][o], my = m[1][o];
-        const float vx = m[2][o] - mx * mx, vy = m[3][o] - my * my, cxy = m[4][o] - mx * my;
-        const float n1 = 2.f * mx * my + kSsimC1, n2 = 2.f * cxy + kSsimC2;
-        const float d1 = mx * mx + my * my + kSsimC1, d2 = vx + vy + kSsimC2;
-        // one reciprocal: 1/den, 1/d1 = d2/den, 1/d2 = d1/den
-        const float rden = 1.0f / (d1 * d2);
-        const float S = n1 * n2 * rden;
-        const float B = -S * (d1 * rden);
-        const float Cm = 2.f * n1 * rden;
-        const float dmx = 2.f * my * n2 * rden - 2.f * mx * S * (d2 * rden);
-        const float A = dmx - 2.f * mx * B - my * Cm;
         const size_t pix = (size_t)gy * W + gx;
+        const bool interior = gx >= kSsimR && gx < W - kSsimR && gy >= kSsimR && gy < H - kSsimR;
+        float A = 0.f, B = 0.f, Cm = 0.f;
+        if (interior) {
+          const float mx = m[0][o], my = m[1][o];
+          const float vx_raw = m[2][o] - mx * mx, vy_raw = m[3][o] - my * my;
+          const float vx = fmaxf(vx_raw, 0.f), vy = fmaxf(vy_raw, 0.f), cxy = m[4][o] - mx * my;
+          const float n1 = 2.f * mx * my + kSsimC1, n2 = 2.f * cxy + kSsimC2;
+          const float d1 = mx * mx + my * my + kSsimC1, d2 = vx + vy + kSsimC2;
+          // one reciprocal: 1/den, 1/d1 = d2/den, 1/d2 = d1/den
+          const float rden = 1.0f / (d1 * d2);
+          const float S = n1 * n2 * rden;
+          // the clamp of var_x at zero passes no gradient where it is active
+          B = vx_raw >= 0.f ? -S * (d1 * rden) : 0.f;
+          Cm = 2.f * n1 * rden;
+          const float dmx = 2.f * my * n2 * rden - 2.f * mx * S * (d2 * rden);
+          A = dmx - 2.f * mx * B - my * Cm;
+          run_ssim += S;
+        }
         maps[(0 + c) * HW + pix] = A;
         maps[(3 + c) * HW + pix] = B;
         maps[(6 + c) * HW + pix] = Cm;
-        run_ssim += S;
-        run_l1 += fabsf(s.x[r + kSsimR][col + kSsimR] - s.y[r + kSsimR][col + kSsimR]);
+        const size_t p3 = pix * 3 + c;
+        run_l1 += fabsf(__ldg(img + p3) - __ldg(ref + p3));
       }
       ssim_sum += (double)run_ssim;
       l1_sum += (double)run_l1;
@@ -218,7 +236,8 @@ __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
 }
 
 __global__ void __launch_bounds__(256) ssim_finalize_kernel(const double* __restrict__ partials,
-                                                            int nblocks, double n, float lambda,
+                                                            int nblocks, double n_ssim,
+                                                            double n_l1, float lambda,
                                                             float* __restrict__ loss,
                                                             float* __restrict__ ssim_out) {
   __shared__ double s_a[256], s_b[256];
@@ -238,7 +257,7 @@ __global__ void __launch_bounds__(256) ssim_finalize_kernel(const double* __rest
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    const double ssim = s_a[0] / n, l1 = s_b[0] / n;
+    const double ssim = s_a[0] / n_ssim, l1 = s_b[0] / n_l1;
     *loss = (float)((1.0 - lambda) * l1 + lambda * (1.0 - ssim));
     if (ssim_out) *ssim_out = (float)ssim;
   }
@@ -247,7 +266,7 @@ __global__ void __launch_bounds__(256) ssim_finalize_kernel(const double* __rest
 __global__ void __launch_bounds__(kSsimThreads, 6) ssim_backward_kernel(
     int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
     const float* __restrict__ maps, const float* __restrict__ grad_loss, float lambda,
-    float inv_n, float* __restrict__ grad_img) {
+    float inv_n_l1, float inv_n_ssim, float* __restrict__ grad_img) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SsimBackwardSmem& s = *reinterpret_cast<SsimBackwardSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -255,7 +274,7 @@ __global__ void __launch_bounds__(kSsimThreads, 6) ssim_backward_kernel(
   const int x0 = bx - kSsimR, y0 = by - kSsimR;
   const size_t HW = (size_t)H * W;
   const float g = __ldg(grad_loss);
-  const float w_l1 = g * (1.0f - lambda) * inv_n, w_ssim = -g * lambda * inv_n;
+  const float w_l1 = g * (1.0f - lambda) * inv_n_l1, w_ssim = -g * lambda * inv_n_ssim;
   const int rb = tid / kSsimTW, col = tid % kSsimTW;
   const int gx = bx + col;
 #pragma unroll 1
@@ -318,10 +337,15 @@ __global__ void __launch_bounds__(kSsimThreads, 6) ssim_backward_kernel(
       const int gy = by + rb * kSsimRun + o;
       if (gx >= W || gy >= H) continue;
       const size_t p = ((size_t)gy * W + gx) * 3 + c;
-      const float xv = __ldg(img + p), yv = __ldg(ref + p);
-      const float d = xv - yv;
+      const float xr = __ldg(img + p), yr = __ldg(ref + p);
+      const float d = xr - yr;
       const float sgn = d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
-      grad_img[p] = w_l1 * sgn + w_ssim * (bl[0][o] + 2.f * xv * bl[1][o] + yv * bl[2][o]);
+      // SSIM sees the clamped images; the clamp passes the gradient where 0 <= x <= 1
+      const float xv = clamp01(xr), yv = clamp01(yr);
+      const float gs = (xr >= 0.f && xr <= 1.f)
+                           ? w_ssim * (bl[0][o] + 2.f * xv * bl[1][o] + yv * bl[2][o])
+                           : 0.f;
+      grad_img[p] = w_l1 * sgn + gs;
     }
     __syncthreads();  // the next channel overwrites the planes
   }
@@ -360,11 +384,14 @@ extern "C" size_t gs_l1_ssim_workspace_size(int H, int W) {
   return (size_t)H * W * 9 * sizeof(float) + ssim_blocks(H, W) * 2 * sizeof(double) + 256;
 }
 
+static double ssim_count(int H, int W) { return 3.0 * (H - 2 * kSsimR) * (W - 2 * kSsimR); }
+
 extern "C" int gs_l1_ssim_forward(int H, int W, const float* img, const float* target,
                                   float lambda_dssim, void* workspace, size_t workspace_bytes,
                                   float* loss, float* ssim_value, void* stream) {
   GS_API_BEGIN();
-  GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
+  GS_REQUIRE(H > 2 * kSsimR && W > 2 * kSsimR,
+             "SSIM needs images of at least 11 x 11 pixels (an 11 x 11 window inside the image)");
   GS_REQUIRE(img && target && workspace && loss, "null pointer");
   GS_REQUIRE(workspace_bytes >= gs_l1_ssim_workspace_size(H, W), "workspace too small");
   const int rc = ensure_gauss();
@@ -379,7 +406,7 @@ extern "C" int gs_l1_ssim_forward(int H, int W, const float* img, const float* t
   cudaStream_t st = (cudaStream_t)stream;
   ssim_forward_kernel<<<grid, kSsimThreads, smem, st>>>(H, W, img, target, maps, partials);
   GS_CHECK_LAUNCH();
-  ssim_finalize_kernel<<<1, 256, 0, st>>>(partials, (int)(grid.x * grid.y),
+  ssim_finalize_kernel<<<1, 256, 0, st>>>(partials, (int)(grid.x * grid.y), ssim_count(H, W),
                                           (double)H * W * 3, lambda_dssim, loss, ssim_value);
   GS_CHECK_LAUNCH();
   return GS_OK;
@@ -391,7 +418,8 @@ extern "C" int gs_l1_ssim_backward(int H, int W, const float* img, const float* 
                                    size_t workspace_bytes, const float* grad_loss,
                                    float* grad_img, void* stream) {
   GS_API_BEGIN();
-  GS_REQUIRE(H > 0 && W > 0, "image height and width must be positive");
+  GS_REQUIRE(H > 2 * kSsimR && W > 2 * kSsimR,
+             "SSIM needs images of at least 11 x 11 pixels (an 11 x 11 window inside the image)");
   GS_REQUIRE(img && target && workspace && grad_loss && grad_img, "null pointer");
   GS_REQUIRE(workspace_bytes >= gs_l1_ssim_workspace_size(H, W), "workspace too small");
   const int rc = ensure_gauss();
@@ -402,7 +430,7 @@ extern "C" int gs_l1_ssim_backward(int H, int W, const float* img, const float* 
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   ssim_backward_kernel<<<grid, kSsimThreads, smem, (cudaStream_t)stream>>>(
       H, W, img, target, static_cast<const float*>(workspace), grad_loss, lambda_dssim,
-      1.0f / (float)((double)H * W * 3), grad_img);
+      (float)(1.0 / ((double)H * W * 3)), (float)(1.0 / ssim_count(H, W)), grad_img);
   GS_CHECK_LAUNCH();
   return GS_OK;
   GS_API_END();

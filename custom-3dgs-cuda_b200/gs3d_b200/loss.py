@@ -1,8 +1,11 @@
 """The training step's photometric loss, 0.8 * L1 + 0.2 * (1 - SSIM), as one autograd op over
 the fused kernels of libgs3d_b200 (gs_l1_ssim_forward / gs_l1_ssim_backward).
 
-`l1_ssim_loss(img, target)` matches `train_step.reconstruction_loss` (the torch formulation:
-11x11 Gaussian window, sigma 1.5, zero padding) on [H, W, 3] fp32 CUDA images.
+`l1_ssim_loss(img, target)` matches the reference's `calculate_loss`
+(gaussian_splatting/utils/loss.py:15-33: torchmetrics SSIM with data_range 1.0 on the images
+clamped to [0, 1], 11x11 Gaussian window, sigma 1.5, mean over the interior positions) and
+`train_step.reconstruction_loss` (its torch formulation) on [H, W, 3] fp32 CUDA images of at
+least 11 x 11 pixels.
 """
 
 from __future__ import annotations

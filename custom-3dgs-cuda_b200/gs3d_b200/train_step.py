@@ -29,26 +29,31 @@ LEARNING_RATES = {"mu": 1.6e-4, "q": 1e-3, "s": 5e-3, "alpha": 5e-2, "A": 2.5e-3
 LAMBDA_DSSIM = 0.2
 
 
-def gaussian_window(size: int = 11, sigma: float = 1.5, device=None) -> torch.Tensor:
-    x = torch.arange(size, dtype=torch.float32, device=device) - (size - 1) / 2.0
+def gaussian_window(size: int = 11, sigma: float = 1.5, device=None,
+                    dtype=torch.float32) -> torch.Tensor:
+    x = torch.arange(size, dtype=dtype, device=device) - (size - 1) / 2.0
     g = torch.exp(-(x * x) / (2.0 * sigma * sigma))
     g = g / g.sum()
     return torch.outer(g, g)
 
 
 def ssim(img: torch.Tensor, ref: torch.Tensor, window: torch.Tensor) -> torch.Tensor:
-    """Mean SSIM of two [H, W, 3] images in [0, 1] with an 11x11 Gaussian window
-    (sigma 1.5), zero padding, C1 = 0.01^2, C2 = 0.03^2."""
-    x = img.permute(2, 0, 1).unsqueeze(0)
-    y = ref.permute(2, 0, 1).unsqueeze(0)
+    """Mean SSIM of two [H, W, 3] images as the reference's loss computes it
+    (gaussian_splatting/utils/loss.py:8-33, torchmetrics structural_similarity_index_measure
+    with data_range=1.0): both images clamped to [0, 1], an 11x11 Gaussian window (sigma 1.5),
+    C1 = 0.01^2, C2 = 0.03^2, variances clamped at 0, the map averaged over the channels and
+    the (H-10) x (W-10) positions whose window lies inside the image. torchmetrics reflect-pads
+    by 5 and crops 5 from each side of the map, which leaves exactly those positions, so the
+    valid (unpadded) convolution below gives the same value."""
+    x = img.permute(2, 0, 1).unsqueeze(0).clamp(0.0, 1.0)
+    y = ref.permute(2, 0, 1).unsqueeze(0).clamp(0.0, 1.0)
     C = x.shape[1]
     w = window.expand(C, 1, *window.shape).contiguous()
-    pad = window.shape[-1] // 2
-    mu_x = F.conv2d(x, w, padding=pad, groups=C)
-    mu_y = F.conv2d(y, w, padding=pad, groups=C)
-    sxx = F.conv2d(x * x, w, padding=pad, groups=C) - mu_x * mu_x
-    syy = F.conv2d(y * y, w, padding=pad, groups=C) - mu_y * mu_y
-    sxy = F.conv2d(x * y, w, padding=pad, groups=C) - mu_x * mu_y
+    mu_x = F.conv2d(x, w, groups=C)
+    mu_y = F.conv2d(y, w, groups=C)
+    sxx = (F.conv2d(x * x, w, groups=C) - mu_x * mu_x).clamp(min=0.0)
+    syy = (F.conv2d(y * y, w, groups=C) - mu_y * mu_y).clamp(min=0.0)
+    sxy = F.conv2d(x * y, w, groups=C) - mu_x * mu_y
     c1, c2 = 0.01 ** 2, 0.03 ** 2
     num = (2 * mu_x * mu_y + c1) * (2 * sxy + c2)
     den = (mu_x * mu_x + mu_y * mu_y + c1) * (sxx + syy + c2)
