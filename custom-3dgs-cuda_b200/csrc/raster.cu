@@ -1,6 +1,7 @@
 // Host orchestration of binning, sorting and blending (gs_rasterize) and of the blend
 // backward (gs_rasterize_backward), with the caller-provided workspace layout.
 #include <algorithm>
+#include <atomic>
 
 #include "binning.cuh"
 #include "blend.cuh"
@@ -83,13 +84,19 @@ RasterLayout make_raster_layout(int N, int W, int H, long long capacity) {
   return L;
 }
 
+// SM count of the current device, looked up once per device ordinal (devices of different
+// models in one process each get their own figure; a racing first lookup stores the same value).
 static int sm_count() {
-  static int count = 0;
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> counts[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
+  int count = counts[dev].load(std::memory_order_relaxed);
   if (count == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
     if (count <= 0) count = 148;
+    counts[dev].store(count, std::memory_order_relaxed);
   }
   return count;
 }

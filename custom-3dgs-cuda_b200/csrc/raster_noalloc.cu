@@ -21,6 +21,14 @@
 // histograms and look-back words it relies on at the start (an asynchronous memset, not an
 // allocation). Calls whose GPU work overlaps — on different streams, or from different host
 // threads — race on the array and must be serialised by the caller.
+//
+// The pair count M is always written to *pair_count_dev (required here, unlike gs_rasterize,
+// because this entry point has no host-side path to report it). When M exceeds
+// pair_capacity the sort, range and blend kernels skip their work, so img, final_T,
+// n_contrib, tile_ranges and sorted_ids are NOT written by that call; the caller must read M
+// and call again with pair_capacity >= M. The cached array address belongs to the device's
+// primary context: after cudaDeviceReset in the same process, do not call this entry point
+// again (the cached address would be stale).
 #include <mutex>
 
 #include "capi_internal.h"
@@ -55,6 +63,8 @@ extern "C" int gs_rasterize_noalloc(int N, int H, int W, const float* depths,
   GS_REQUIRE(img && tile_ranges && final_T && n_contrib, "null output pointer");
   GS_REQUIRE(N == 0 || (depths && mean2d && cov2d && colors && alpha), "null input pointer");
   GS_REQUIRE(pair_capacity == 0 || sorted_ids, "null sorted_ids with a non-zero capacity");
+  GS_REQUIRE(pair_count_dev, "pair_count_dev is required: it reports M, and M > pair_capacity "
+             "leaves the outputs unwritten");
   const RasterLayout L = make_raster_layout(N, W, H, pair_capacity);
   if (L.total > kNoAllocScratchBytes)
     return set_error(GS_ERR_CAPACITY,

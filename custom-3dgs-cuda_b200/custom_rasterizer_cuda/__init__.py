@@ -38,6 +38,8 @@ __all__ = [
 ]
 
 TILE = 16
+# largest pair capacity the C ABI accepts (gs_rasterize requires pair_capacity < 2^30)
+_MAX_PAIRS = (1 << 30) - 1
 
 
 # ---- input checks (csrc/cuda_check.h:24-47) ------------------------------------------------
@@ -248,6 +250,10 @@ def rasterize(num_gaussians, depths, mean_2d, cov_2d, colors, alpha, height, wid
             _capacity.update(N, H, W, M)
             if M <= cap:
                 return img, sorted_ids[:M], tile_ranges, final_T, n_contrib
+            if M > _MAX_PAIRS:
+                raise RuntimeError(
+                    f"rasterize: {M} (tile, Gaussian) pairs exceed the supported maximum of "
+                    f"{_MAX_PAIRS}; reduce the number of Gaussians or the image size")
             cap = M
         raise RuntimeError("pair count kept growing between attempts")
 

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _capacity, _m_event, _ptr, _stream, _tiles
+from . import _MAX_PAIRS, _capacity, _m_event, _ptr, _stream, _tiles
 from ._lib import check, lib
 
 
@@ -72,6 +72,10 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
                 state = RenderState(ws, cap, sorted_ids, M, tile_ranges, final_T, n_contrib, H, W,
                                     flags & 2)
                 return img, radii, state
+            if M > _MAX_PAIRS:
+                raise RuntimeError(
+                    f"render: {M} (tile, Gaussian) pairs exceed the supported maximum of "
+                    f"{_MAX_PAIRS}; reduce the number of Gaussians or the image size")
             cap = M
     raise RuntimeError("pair count kept growing between attempts")
 

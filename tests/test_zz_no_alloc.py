@@ -64,8 +64,72 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(crc, cuda_de
         assert torch.equal(ids[:M], ids_r)
         assert torch.equal(ranges, ranges_r)
         assert torch.equal(n_contrib, nc_r)
-        np.testing.assert_allclose(final_T.cpu().numpy(), T_r.cpu().numpy(), rtol=1e-5, atol=1e-6)
-        np.testing.assert_allclose(img.cpu().numpy(), img_r.cpu().numpy(), rtol=1e-5, atol=1e-6)
+        # the same kernels run in both entry points, so the blend is bit-identical
+        assert torch.equal(final_T, T_r)
+        assert torch.equal(img, img_r)
+    assert crc.device_error_bits() == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_overflow_reports_m_and_a_retry_matches(crc, cuda_device):
+    """A capacity below M: the call still returns GS_OK and reports M through pair_count_dev
+    (the outputs are not written); a second call with capacity M matches gs_rasterize."""
+    from custom_rasterizer_cuda import _lib
+    from gs3d_b200 import scenes
+
+    dev = cuda_device
+    sc = scenes.config2(6, n=20_000)
+    view = scenes.pinhole((0.0, 0.0, 8.0), 320, 200, 250.0)
+    H, W = view.height, view.width
+    inp = _inputs(crc, sc, view, dev)
+    img_r, ids_r, ranges_r, T_r, nc_r = crc.rasterize(sc.N, *inp, H, W)
+    M = ids_r.numel()
+    assert M > 100
+    rc, *_, m = _noalloc(_lib.lib, sc.N, H, W, *inp, M // 3, dev)
+    assert rc == _lib.GS_OK and m == M
+    rc, img, ids, ranges, final_T, n_contrib, m = _noalloc(_lib.lib, sc.N, H, W, *inp, M, dev)
+    assert rc == _lib.GS_OK and m == M
+    assert torch.equal(ids, ids_r) and torch.equal(ranges, ranges_r)
+    assert torch.equal(n_contrib, nc_r) and torch.equal(final_T, T_r) and torch.equal(img, img_r)
+    assert crc.device_error_bits() == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_zero_gaussians_and_a_layout_just_under_the_limit(crc, cuda_device):
+    """N == 0 gives the reference's empty render (zero image, final_T = 1, zero ranges and
+    counts) even after a call that left other contents in the shared scratch; a layout within
+    64 KiB of the 16 MiB limit is accepted and matches gs_rasterize."""
+    from custom_rasterizer_cuda import _lib
+    from gs3d_b200 import scenes
+
+    dev = cuda_device
+    L = _lib.lib
+    z = torch.zeros((0, 3), device=dev)
+    rc, img, ids, ranges, final_T, n_contrib, m = _noalloc(L, 0, 40, 70, z, z, z, z, z, 16, dev)
+    assert rc == _lib.GS_OK and m == 0
+    assert float(img.abs().sum()) == 0.0 and bool((final_T == 1).all())
+    assert int(ranges.abs().sum()) == 0 and int(n_contrib.abs().sum()) == 0
+
+    limit = 16 << 20
+    sc = scenes.config2(7, n=65_536)
+    view = scenes.pinhole((0.0, 0.0, 8.0), 1024, 1024, 800.0)
+    H, W = view.height, view.width
+    lo, hi = 0, 1 << 24  # largest pair capacity whose layout fits the fixed scratch
+    while hi - lo > 1:
+        mid = (lo + hi) // 2
+        lo, hi = (mid, hi) if L.gs_rasterize_workspace_size(sc.N, H, W, mid) <= limit else (lo, mid)
+    cap = lo
+    assert limit - L.gs_rasterize_workspace_size(sc.N, H, W, cap) < 64 << 10
+    inp = _inputs(crc, sc, view, dev)
+    img_r, ids_r, ranges_r, T_r, nc_r = crc.rasterize(sc.N, *inp, H, W)
+    M = ids_r.numel()
+    assert 0 < M <= cap
+    rc, img, ids, ranges, final_T, n_contrib, m = _noalloc(L, sc.N, H, W, *inp, cap, dev)
+    assert rc == _lib.GS_OK, L.gs_last_error()
+    assert m == M and torch.equal(ids[:M], ids_r) and torch.equal(ranges, ranges_r)
+    assert torch.equal(n_contrib, nc_r) and torch.equal(final_T, T_r) and torch.equal(img, img_r)
+    rc, *_ = _noalloc(L, sc.N, H, W, *inp, cap + 4096, dev)
+    assert rc == _lib.GS_ERR_CAPACITY
     assert crc.device_error_bits() == 0
 
 
@@ -75,7 +139,18 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
 
     L = _lib.lib
     rc = L.gs_rasterize_noalloc(1_000_000, 1080, 1920, 1, 1, 1, 1, 1, 8_000_000, 1, 1, 1, 1, 1,
-                                None, None)
+                                1, None)
     assert rc == _lib.GS_ERR_CAPACITY
     msg = L.gs_last_error().decode()
     assert "fixed scratch holds 16777216 bytes" in msg and "gs_rasterize" in msg
+
+
+def test_noalloc_requires_the_pair_count_pointer():
+    """Without pair_count_dev a caller could not tell an overflowed call (outputs unwritten)
+    from a complete one, so NULL is rejected on the host."""
+    from custom_rasterizer_cuda import _lib
+
+    L = _lib.lib
+    rc = L.gs_rasterize_noalloc(16, 32, 32, 1, 1, 1, 1, 1, 64, 1, 1, 1, 1, 1, None, None)
+    assert rc == _lib.GS_ERR_INVALID_ARG
+    assert "pair_count_dev" in L.gs_last_error().decode()
