@@ -357,3 +357,43 @@ extern "C" int gs_adc_apply(int N, const void* workspace, size_t workspace_bytes
   return GS_OK;
   GS_API_END();
 }
+
+// ---- densification statistics of one view (the reference trainer's
+// accumulate_densification_stats, gaussian_splatting/utils/adc.py:58-80) ----
+namespace gs {
+
+// One thread per Gaussian: n = |(gx * sx, gy * sy)| of its screen-space mean gradient; where
+// n > 0, norm_sum += n and count += 1; norm_max = max(norm_max, n) when given.
+__global__ void __launch_bounds__(256) densify_stats_kernel(int N, const float* __restrict__ g2,
+                                                            int g_stride, float sx, float sy,
+                                                            float* __restrict__ norm_sum,
+                                                            float* __restrict__ count,
+                                                            float* __restrict__ norm_max) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const float gx = __ldg(g2 + (size_t)i * g_stride) * sx;
+  const float gy = __ldg(g2 + (size_t)i * g_stride + 1) * sy;
+  const float n = sqrtf(gx * gx + gy * gy);
+  if (n > 0.f) {
+    norm_sum[i] += n;
+    count[i] += 1.f;
+  }
+  if (norm_max) norm_max[i] = fmaxf(norm_max[i], n);
+}
+
+}  // namespace gs
+
+extern "C" int gs_densify_stats(int N, const float* mean2d_grad, int grad_stride, float scale_x,
+                                float scale_y, float* norm_sum, float* count, float* norm_max,
+                                void* stream) {
+  GS_API_BEGIN();
+  GS_REQUIRE(N >= 0, "N must be non-negative");
+  GS_REQUIRE(grad_stride >= 2, "the gradient rows need at least two floats");
+  if (N == 0) return GS_OK;
+  GS_REQUIRE(mean2d_grad && norm_sum && count, "null pointer");
+  densify_stats_kernel<<<(N + 255) / 256, 256, 0, (cudaStream_t)stream>>>(
+      N, mean2d_grad, grad_stride, scale_x, scale_y, norm_sum, count, norm_max);
+  GS_CHECK_LAUNCH();
+  return GS_OK;
+  GS_API_END();
+}

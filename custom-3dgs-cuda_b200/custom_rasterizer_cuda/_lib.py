@@ -61,6 +61,7 @@ SIGNATURES = {
     "gs_adc_plan": (c_int, [c_int, P, P, P, P, P, c_float, c_float, c_float, c_float, c_float,
                             c_int, c_int, P, c_size_t, P, P, P]),
     "gs_adc_apply": (c_int, [c_int, P, c_size_t, P, P, P, P, P, c_int, P, P, P, P]),
+    "gs_densify_stats": (c_int, [c_int, P, c_int, c_float, c_float, P, P, P, P]),
     "gs_event_create": (c_int, [POINTER(c_void_p)]),
     "gs_event_synchronize": (c_int, [P]),
     "gs_event_destroy": (c_int, [P]),

@@ -27,72 +27,85 @@ from torch.nn import Parameter
 
 from gaussian_splatting.scene.gaussian import gaussian
 
-_GROUP_TO_ATTR = {
-    "mu": "mu",
-    "q": "q",
-    "Scale": "s",
-    "Opacity": "alpha",
-    "Albedo Coefficient": "A",
-    "Illumination Coefficients": "k_j",
-}
-_ORDER = ("mu", "q", "s", "alpha", "A", "k_j")
+# The reference optimizer's group names (its setup_optimizer) and the Gaussian attribute each
+# one holds: the names are the optimizer's interface, so they are kept.
+_GROUPS = (("mu", "mu"), ("q", "q"), ("Scale", "s"), ("Opacity", "alpha"),
+           ("Albedo Coefficient", "A"), ("Illumination Coefficients", "k_j"))
+_GROUP_TO_ATTR = dict(_GROUPS)
+_ORDER = tuple(attr for _, attr in _GROUPS)
+
+# densification buffers and the trailing shape of each
+_STATE_BUFFERS = (("xyz_grad_accum", (1,)), ("denom", (1,)), ("max_radii2D", ()))
 
 
 def scene_extent_from_means(mu: t.Tensor) -> float:
-    mins = mu.min(dim=0).values
-    maxs = mu.max(dim=0).values
-    return max(float((maxs - mins).norm().item()), 1e-3)
+    """Length of the diagonal of the means' bounding box (at least 1e-3)."""
+    lo, hi = t.aminmax(mu, dim=0)
+    return max(float(t.linalg.vector_norm(hi - lo)), 1e-3)
 
 
 def scene_extent_from_cameras(cameras) -> float:
-    centers = -t.bmm(cameras.R.transpose(1, 2), cameras.t.unsqueeze(-1)).squeeze(-1)
-    center = centers.mean(dim=0)
-    return max(float((centers - center).norm(dim=-1).max().item()) * 1.1, 1e-3)
+    """1.1 x the largest distance of a camera centre (-R^T t) from the centres' mean (at
+    least 1e-3)."""
+    centres = -t.einsum("nji,nj->ni", cameras.R, cameras.t)
+    spread = t.linalg.vector_norm(centres - centres.mean(dim=0, keepdim=True), dim=1)
+    return max(1.1 * float(spread.max()), 1e-3)
 
 
 def ensure_densification_state(gaussians: gaussian) -> None:
     """Densification buffers (xyz_grad_accum [N,1], denom [N,1], max_radii2D [N]) allocated or
-    resized to N, keeping their prefix."""
+    resized to the current N: rows that survive keep their values, new rows start at zero."""
     n = int(gaussians.mu.shape[0])
-    dev, dt = gaussians.mu.device, gaussians.mu.dtype
-
-    def fit(buf, rest):
-        if buf is not None and buf.shape[0] == n:
-            return buf
-        out = t.zeros((n, *rest), device=dev, dtype=dt)
-        if buf is not None:
-            m = min(int(buf.shape[0]), n)
-            out[:m] = buf[:m]
-        return out
-
-    gaussians.xyz_grad_accum = fit(getattr(gaussians, "xyz_grad_accum", None), (1,))
-    gaussians.denom = fit(getattr(gaussians, "denom", None), (1,))
-    gaussians.max_radii2D = fit(getattr(gaussians, "max_radii2D", None), ()).view(n)
+    for name, tail in _STATE_BUFFERS:
+        cur = getattr(gaussians, name, None)
+        if cur is None or int(cur.shape[0]) != n:
+            fresh = gaussians.mu.new_zeros((n, *tail))
+            if cur is not None:
+                keep = min(int(cur.shape[0]), n)
+                fresh[:keep] = cur[:keep].reshape(keep, *tail)
+            cur = fresh
+        setattr(gaussians, name, cur.reshape(n, *tail))
 
 
 def accumulate_densification_stats(gaussians: gaussian, mean2d_grad: t.Tensor | None = None, *,
                                    width: int | None = None, height: int | None = None) -> None:
+    """Adds one view's screen-space gradient norms |dL/dmean2d * (W/2, H/2)| to xyz_grad_accum
+    and counts them in denom, for Gaussians with a non-zero norm (the scale is 1 when the image
+    size is not given). One library launch (gs_densify_stats) on the gradient's device."""
     if mean2d_grad is None or mean2d_grad.shape[0] != gaussians.mu.shape[0]:
         return
     ensure_densification_state(gaussians)
-    g = mean2d_grad[:, :2].detach()
-    if width is not None and height is not None and width > 0 and height > 0:
-        g = g * t.tensor([width / 2.0, height / 2.0], device=g.device, dtype=g.dtype)
-    norm = t.norm(g, dim=-1, keepdim=True)
-    visible = norm.squeeze(-1) > 0
-    gaussians.xyz_grad_accum[visible] += norm[visible]
-    gaussians.denom[visible] += 1.0
+    if not mean2d_grad.is_cuda:
+        raise RuntimeError("accumulate_densification_stats needs CUDA tensors")
+    grad = mean2d_grad.detach().float()
+    if grad.stride(-1) != 1 or grad.dim() != 2:
+        grad = grad.reshape(grad.shape[0], -1).contiguous()
+    sized = bool(width and height and width > 0 and height > 0)
+    sx, sy = (width / 2.0, height / 2.0) if sized else (1.0, 1.0)
+    from custom_rasterizer_cuda import _lib
+
+    n = int(grad.shape[0])
+    acc, den = gaussians.xyz_grad_accum, gaussians.denom
+    if not (acc.is_contiguous() and den.is_contiguous()):
+        raise RuntimeError("the densification buffers must be contiguous")
+    with t.cuda.device(grad.device):
+        _lib.check(_lib.lib.gs_densify_stats(
+            n, grad.data_ptr(), grad.stride(0), float(sx), float(sy), acc.data_ptr(),
+            den.data_ptr(), None, t.cuda.current_stream(grad.device).cuda_stream))
 
 
 def update_max_radii2d(gaussians: gaussian, radii: t.Tensor | None) -> None:
+    """Running per-Gaussian maximum of the screen radius."""
     if radii is None or radii.shape[0] != gaussians.mu.shape[0]:
         return
     ensure_densification_state(gaussians)
-    gaussians.max_radii2D = t.maximum(gaussians.max_radii2D, radii.detach())
+    gaussians.max_radii2D = radii.detach().maximum(gaussians.max_radii2D)
 
 
 def clamp_log_scales(gaussians: gaussian, scene_extent: float) -> None:
-    gaussians.s.data.clamp_(max=math.log(max(0.1 * scene_extent, 1e-7)))
+    """Caps every log-scale at log(0.1 x the scene extent) (floor 1e-7 before the log)."""
+    cap = math.log(max(scene_extent * 0.1, 1e-7))
+    gaussians.s.data.clamp_(max=cap)
 
 
 def _group_state(optimizer, name):

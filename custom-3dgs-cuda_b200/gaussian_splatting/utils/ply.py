@@ -21,6 +21,7 @@ from pathlib import Path
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 from gaussian_splatting.scene.gaussian import gaussian
 
@@ -38,32 +39,42 @@ def ply_property_names(max_sh_degree: int = 3) -> list[str]:
 
 
 def pack_inria(gaussians: gaussian, max_sh_degree: int = 3) -> torch.Tensor:
-    """[N, 62] float32 rows in the file's property order, on the parameters' device."""
+    """[N, 62] float32 rows in the file's property order, built on the parameters' device.
+
+    The rows are allocated once and each property group is written into its own column block;
+    the SH rest block is viewed as [N, 3, K] so the channel-major order comes from the
+    destination's layout (missing bands stay zero, extra bands are dropped)."""
     n_rest = (max_sh_degree + 1) ** 2 - 1
     with torch.no_grad():
-        xyz = gaussians.mu.detach().float().reshape(-1, 3)
-        n = int(xyz.shape[0])
-        dev = xyz.device
-        f_dc = gaussians.A.detach().float().reshape(n, 3)
-        rest = gaussians.k_j.detach().float()
-        if rest.ndim != 3 or rest.shape[-1] != 3:
-            raise ValueError(f"Expected k_j shape (N, K, 3), got {tuple(rest.shape)}")
-        if rest.shape[1] < n_rest:
-            rest = torch.cat([rest, torch.zeros(n, n_rest - rest.shape[1], 3, device=dev)], 1)
-        elif rest.shape[1] > n_rest:
-            rest = rest[:, :n_rest, :]
-        f_rest = rest.transpose(1, 2).reshape(n, 3 * n_rest)
-        alpha = gaussians.alpha.detach().float().reshape(n, 1)
-        if n > 0 and bool(((alpha > 0.0) & (alpha < 1.0)).all()) and float(alpha.min()) > 1e-6:
-            a = alpha.clamp(1e-6, 1.0 - 1e-6)
-            opacity = torch.log(a / (1.0 - a))
-        else:
-            opacity = alpha
-        scale = gaussians.s.detach().float().reshape(n, 3)
-        quat = gaussians.q.detach().float().reshape(n, 4)
-        quat = quat / quat.norm(dim=-1, keepdim=True).clamp_min(1e-8)
-        normals = torch.zeros(n, 3, device=dev)
-        return torch.cat([xyz, normals, f_dc, f_rest, opacity, scale, quat], dim=1).contiguous()
+        mu = gaussians.mu.detach().float()
+        n = int(mu.numel() // 3)
+        sh = gaussians.k_j.detach().float()
+        if sh.dim() != 3 or sh.shape[2] != 3:
+            raise ValueError(f"k_j must be [N, K, 3] spherical-harmonic coefficients, got shape "
+                             f"{tuple(sh.shape)}")
+        rows = torch.zeros((n, 6 + 3 + 3 * n_rest + 1 + 3 + 4), device=mu.device)
+        c = 0
+
+        def block(width: int) -> torch.Tensor:
+            nonlocal c
+            view = rows[:, c:c + width]
+            c += width
+            return view
+
+        block(3).copy_(mu.reshape(n, 3))
+        block(3)  # normals: zero
+        block(3).copy_(gaussians.A.detach().float().reshape(n, 3))
+        k = min(int(sh.shape[1]), n_rest)
+        block(3 * n_rest).view(n, 3, n_rest)[:, :, :k] = sh[:, :k, :].transpose(1, 2)
+        alpha = gaussians.alpha.detach().float().reshape(n)
+        legacy = False
+        if n > 0:
+            lo, hi = torch.aminmax(alpha)
+            legacy = float(lo) > 1e-6 and float(hi) < 1.0  # probabilities, not logits
+        block(1)[:, 0] = torch.logit(alpha, eps=1e-6) if legacy else alpha
+        block(3).copy_(gaussians.s.detach().float().reshape(n, 3))
+        block(4).copy_(F.normalize(gaussians.q.detach().float().reshape(n, 4), dim=1, eps=1e-8))
+        return rows
 
 
 def _header(n: int, names: list[str]) -> bytes:

@@ -159,3 +159,43 @@ def test_device_adc_no_densify_and_optimizer_steps(cuda_device):
     for name in NAMES:
         p, st = group_state(opt, name)
         assert st["exp_avg"].shape == p.shape and torch.isfinite(p).all()
+
+
+def test_densification_statistics_helpers(cuda_device):
+    """accumulate_densification_stats (one gs_densify_stats launch) against the reference
+    helper's semantics (gaussian_splatting/utils/adc.py:58-80), restated with torch ops: the
+    norm of the screen-space mean gradient scaled by (W/2, H/2) added where it is non-zero,
+    counted in denom; with buffers grown from a shorter set (prefix kept, new rows zero), a
+    [N, 3] gradient (only the first two columns used) and no image size (scale 1)."""
+    from gaussian_splatting.scene.gaussian import gaussian
+    from gaussian_splatting.utils.adc import (accumulate_densification_stats,
+                                              ensure_densification_state, update_max_radii2d)
+
+    dev = cuda_device
+    g = torch.Generator("cpu").manual_seed(21)
+    n = 5000
+    gs = gaussian(n)
+    gs.mu = torch.randn(n, 3, generator=g).to(dev)
+    gs.xyz_grad_accum = torch.rand(n - 100, 1, generator=g).to(dev)
+    gs.denom = torch.full((n - 100, 1), 2.0).to(dev)
+    gs.max_radii2D = torch.rand(n - 100, generator=g).to(dev)
+    ensure_densification_state(gs)
+    assert gs.xyz_grad_accum.shape == (n, 1) and gs.max_radii2D.shape == (n,)
+    assert float(gs.xyz_grad_accum[n - 100:].abs().sum()) == 0.0
+    acc, den = gs.xyz_grad_accum.clone(), gs.denom.clone()
+    grad = torch.randn(n, 3, generator=g)
+    grad[::7] = 0.0  # not visible in this view
+    grad = grad.to(dev)
+    for width, height in ((1920, 1080), (None, None)):
+        accumulate_densification_stats(gs, grad, width=width, height=height)
+        scale = torch.tensor([width / 2.0, height / 2.0] if width else [1.0, 1.0], device=dev)
+        norm = torch.norm(grad[:, :2] * scale, dim=-1, keepdim=True)
+        vis = norm.squeeze(-1) > 0
+        acc[vis] += norm[vis]
+        den[vis] += 1.0
+        torch.testing.assert_close(gs.xyz_grad_accum, acc, rtol=1e-6, atol=0)
+        assert torch.equal(gs.denom, den)
+    radii = torch.rand(n, generator=g).to(dev)
+    before = gs.max_radii2D.clone()
+    update_max_radii2d(gs, radii)
+    assert torch.equal(gs.max_radii2D, torch.maximum(before, radii))
