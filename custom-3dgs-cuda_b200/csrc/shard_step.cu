@@ -15,8 +15,9 @@
 // 1 / batch) with this rank's shard of the moments; statistic groups are written back reduced.
 // The max statistic (non-negative floats, ordered like their u32 bit patterns) is reduced with
 // multimem.ld_reduce.max.u32 or peer loads. A closing barrier makes every rank's stores visible
-// everywhere before the kernel ends. Barrier waits are bounded (5 s of wall time, and an
-// iteration cap); a timeout sets kErrPeerTimeout and the kernel returns.
+// everywhere before the kernel ends. Barrier waits are bounded (gs_shard_buffers::wait_ns of
+// GPU global time, 5 s by default, and an iteration cap); a timeout sets kErrPeerTimeout and
+// the kernel returns.
 #include <algorithm>
 #include <cmath>
 
@@ -92,7 +93,7 @@ __device__ __forceinline__ unsigned cas_acquire_sys(unsigned* p, unsigned cmp, u
   return old;
 }
 
-constexpr unsigned long long kPeerWaitNs = 5000000000ull;  // 5 s per barrier wait
+constexpr unsigned long long kPeerWaitNs = 5000000000ull;  // default limit of a barrier wait
 constexpr unsigned kPeerSpinLimit = 1u << 26;                // and never more iterations
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -118,14 +119,15 @@ __device__ bool peer_barrier(const ShardArgs& a) {
     unsigned* in = pads[rank] + slot + peer;
     unsigned spins = 0;
     bool ok = true;
+    const unsigned long long limit = a.b.wait_ns ? a.b.wait_ns : kPeerWaitNs;
     const unsigned long long t0 = global_ns();
     __threadfence_system();
     while (cas_release_sys(out, 0u, 1u) != 0u) {
-      if (++spins > kPeerSpinLimit || global_ns() - t0 > kPeerWaitNs) { ok = false; break; }
+      if (++spins > kPeerSpinLimit || global_ns() - t0 > limit) { ok = false; break; }
       __nanosleep(64);
     }
     while (ok && cas_acquire_sys(in, 1u, 0u) != 1u) {
-      if (++spins > kPeerSpinLimit || global_ns() - t0 > kPeerWaitNs) { ok = false; break; }
+      if (++spins > kPeerSpinLimit || global_ns() - t0 > limit) { ok = false; break; }
       __nanosleep(64);
     }
     if (!ok) {

@@ -62,7 +62,7 @@ class ShardBuffers(ctypes.Structure):
                 ("params", c_void_p), ("params_mc", c_void_p), ("params_peers", c_void_p),
                 ("maxbuf", c_void_p), ("max_mc", c_void_p), ("max_peers", c_void_p),
                 ("signal_pads", c_void_p), ("signal_slots", c_longlong),
-                ("phase_ns", c_void_p)]
+                ("phase_ns", c_void_p), ("wait_ns", ctypes.c_ulonglong)]
 
 
 class ShardedStep:

@@ -92,9 +92,13 @@ GS_API int gs_rasterize(int N, int H, int W, const float* depths, const float* m
  * Binning/sort scratch comes from a 16 MiB array compiled into the library (held on every
  * device that loads it); calls whose layout for (N, H, W, pair_capacity) does not fit return
  * GS_ERR_CAPACITY before any GPU work. The first call on a device looks the array's address up
- * (cudaGetSymbolAddress), so make it before any stream capture. Calls share the array: GPU
- * work of overlapping calls races and must be serialised by the caller. Outputs and M (into
- * *pair_count_dev when non-NULL) as gs_rasterize; nothing is allocated.
+ * (cudaGetSymbolAddress), so make it before any stream capture, and do not call it again after
+ * cudaDeviceReset in the same process (the cached address would be stale). Calls share the
+ * array: GPU work of overlapping calls races and must be serialised by the caller. Outputs as
+ * gs_rasterize; nothing is allocated. `pair_count_dev` is REQUIRED (a device int; NULL is
+ * GS_ERR_INVALID_ARG): it receives M, and when M > pair_capacity the call writes none of img,
+ * final_T, n_contrib, tile_ranges or sorted_ids (status GS_OK, the overflow is only known on
+ * the device), so the caller must read M and call again with pair_capacity >= M.
  */
 GS_API int gs_rasterize_noalloc(int N, int H, int W, const float* depths, const float* mean2d,
                                 const float* cov2d, const float* colors, const float* alpha,
@@ -201,8 +205,12 @@ GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const 
 /*
  * Fused photometric loss of the training step (no counterpart in the reference's extension;
  * the reference trainer computes it with torchmetrics, gaussian_splatting/utils/loss.py:12-33):
- * loss = (1 - lambda) * mean|img - target| + lambda * (1 - SSIM), SSIM with an 11x11 Gaussian
- * window (sigma 1.5), zero padding, C1 = 0.01^2, C2 = 0.03^2, over [H, W, 3] images.
+ * loss = (1 - lambda) * mean|img - target| + lambda * (1 - SSIM) over [H, W, 3] images, with
+ * the reference's SSIM semantics (torchmetrics structural_similarity_index_measure, data_range
+ * 1.0, on the images clamped to [0, 1]): 11x11 Gaussian window (sigma 1.5), C1 = 0.01^2,
+ * C2 = 0.03^2, variances clamped at 0, mean over the channels and the (H-10) x (W-10) interior
+ * (torchmetrics reflect-pads by 5 and crops the same border, so the padding never reaches the
+ * value). H and W must be at least 11. The L1 term uses the unclamped images.
  * The forward writes the scalar loss (and the mean SSIM when ssim_value is non-NULL) to device
  * memory and leaves per-pixel derivative maps in the workspace for the backward, which writes
  * grad_img = dL/dimg scaled by *grad_loss (a device scalar).
@@ -269,6 +277,9 @@ typedef struct gs_shard_buffers {
      earliest CTA start, the latest end of the opening barrier, of the data loop and of the
      closing barrier (initialise to {~0, 0, 0, 0}) */
   unsigned long long* phase_ns;
+  /* limit of each barrier wait in nanoseconds of GPU global time (0: 5 s); a wait that runs
+     out sets bit 8 of gs_device_error_bits and the kernel returns */
+  unsigned long long wait_ns;
 } gs_shard_buffers;
 
 GS_API int gs_sharded_adam_step(const gs_shard_buffers* buffers, float* exp_avg,
@@ -311,6 +322,17 @@ GS_API int gs_adc_apply(int N, const void* workspace, size_t workspace_bytes,
                         float* const* out_exp_avg, float* const* out_exp_avg_sq, void* stream);
 
 /*
+ * Densification statistics of one rendered view: the reference trainer's
+ * accumulate_densification_stats (gaussian_splatting/utils/adc.py:58-80) in one launch. For each
+ * Gaussian i with screen-space mean gradient (g[i*grad_stride], g[i*grad_stride+1]),
+ * n = |(gx * scale_x, gy * scale_y)|; where n > 0, norm_sum[i] += n and count[i] += 1;
+ * norm_max[i] = max(norm_max[i], n) when norm_max is non-NULL.
+ */
+GS_API int gs_densify_stats(int N, const float* mean2d_grad, int grad_stride, float scale_x,
+                            float scale_y, float* norm_sum, float* count, float* norm_max,
+                            void* stream);
+
+/*
  * CUDA event helpers for m_ready_event (cudaEvent_t values passed as void*): create an event
  * with timing disabled, block the calling thread until it completes, destroy it.
  */
@@ -337,7 +359,8 @@ GS_API unsigned long long gs_kernel_launches(void);
 /*
  * Device-side error bits recorded by the kernels of earlier calls on this device since
  * the last gs_clear_device_errors() (1 = a look-back wait gave up, 2 = pair capacity
- * exceeded, 4 = an index out of range). Synchronises the device.
+ * exceeded, 4 = an index out of range, 8 = a cross-GPU barrier wait of gs_sharded_adam_step
+ * gave up). Synchronises the device.
  */
 GS_API int gs_device_error_bits(unsigned* bits);
 GS_API int gs_clear_device_errors(void);
