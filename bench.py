@@ -286,6 +286,7 @@ def render_table(dev, reps: int = 10, only=None) -> dict:
         return r, (a, b)
 
     def fwd_bwd(g, view):
+        work = scene_work(g, view)
         fw, bw = [], []
         for i in range(reps + 2):
             for name in PARAM_NAMES:
@@ -307,9 +308,12 @@ def render_table(dev, reps: int = 10, only=None) -> dict:
 
             _, ev = timed(frames)
             torch.cuda.synchronize()
-        return {"fwd_ms": statistics.median(fw), "bwd_ms": statistics.median(bw),
-                "fps": reps / (ev[0].elapsed_time(ev[1]) * 1e-3)}
+        res = {"fwd_ms": statistics.median(fw), "bwd_ms": statistics.median(bw),
+               "fps": reps / (ev[0].elapsed_time(ev[1]) * 1e-3)}
+        res.update(render_roofline(work, res["fwd_ms"], res["bwd_ms"], pk))
+        return res
 
+    pk = peaks()
     out = {}
     want = (lambda name: only is None or name in only)
     if want("config0"):
@@ -345,8 +349,130 @@ def render_table(dev, reps: int = 10, only=None) -> dict:
         _, ev = timed(sweep)
         torch.cuda.synchronize()
     ms = ev[0].elapsed_time(ev[1])
-    out["config3_3M_3840x2160_32_cameras"] = {"fps": len(views3) / (ms * 1e-3),
-                                              "fwd_ms_per_frame": ms / len(views3)}
+    work = [scene_work(g3, v) for v in views3[::8]]
+    mean_work = {k: statistics.mean(w[k] for w in work) for k in work[0]}
+    res = {"fps": len(views3) / (ms * 1e-3), "fwd_ms_per_frame": ms / len(views3)}
+    res.update(render_roofline(mean_work, ms / len(views3), None, pk))
+    out["config3_3M_3840x2160_32_cameras"] = res
+    return out
+
+
+def scene_work(g, view) -> dict:
+    """Units of work of one render of `view` through the fused path with the reference's
+    binning (what RasterizeFunction runs): N Gaussians, P pixels, T tiles, M pairs, the
+    (pixel, Gaussian) pairs an exact front-to-back blend must test (sum of n_contrib: each
+    pixel's list walked to its last contributor) and E_f as the reference's blend evaluates
+    them (every pixel of a tile tests each record until the whole tile is done, checked once per
+    256-record batch: sum over tiles of 256 * min(K_t, ceil((max_p n_contrib_p + 1) / 256) *
+    256), K_t the tile's list length)."""
+    from custom_rasterizer_cuda.render import render_forward
+
+    with torch.no_grad():
+        op = torch.sigmoid(g.alpha.detach()).reshape(-1).contiguous()
+        R, t = view["R"], view["T"]
+        cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+        _, _, st = render_forward(g.mu.detach(), g.q.detach(), g.s.detach(), op, g.A.detach(),
+                                  g.k_j.detach(), R, t, cam, view["fx"], view["fy"], view["cx"],
+                                  view["cy"], view["height"], view["width"])
+        H, W = view["height"], view["width"]
+        tx, ty = (W + 15) // 16, (H + 15) // 16
+        nc = st.n_contrib
+        pad = torch.zeros((ty * 16, tx * 16), dtype=nc.dtype, device=nc.device)
+        pad[:H, :W] = nc
+        tile_max = pad.view(ty, 16, tx, 16).amax(dim=(1, 3)).reshape(-1).to(torch.int64)
+        ranges = st.tile_ranges.to(torch.int64)
+        K = ranges[:, 1] - ranges[:, 0]
+        reach = torch.div(tile_max + 1 + 255, 256, rounding_mode="floor") * 256
+        e_f = int((256 * torch.minimum(K, reach)).sum())
+        return {"N": int(g.mu.shape[0]), "P": H * W, "T": tx * ty, "M": int(st.pairs),
+                "sum_n_contrib": int(nc.to(torch.int64).sum()), "E_f": e_f}
+
+
+# Algorithmic bytes of the HBM-bound stages of one fused render (RasterizeFunction), per unit:
+# forward: parameters in (236 B/G) + blend record, rect and depth key out (48 + 8 + 8 B/G), the
+# depth sort's four passes over 16 B/G, duplication (12 B/G in, 8 B per pair out), the tile
+# sort's passes over 16 B per pair, the ranges (8 B per pair) and the image, transmittance and
+# contributor count out (20 B per pixel); backward: the upstream image gradient, transmittance
+# and counts in (20 B per pixel), then parameters, records and blend sums in (236 + 48 + 40
+# B/G) and gradients out (236 B/G). FP32 work of the blends per tested pair: 14 flops forward,
+# 40 flops backward.
+def render_roofline(work: dict, fwd_ms: float, bwd_ms: float | None, pk: dict) -> dict:
+    N, M, P, T = work["N"], work["M"], work["P"], work["T"]
+    tile_passes = max(1, math.ceil(math.log2(max(T, 2)) / 8))
+    fwd_bytes = (236 + 64) * N + 4 * 16 * N + 12 * N + 8 * M + tile_passes * 16 * M + 8 * M + 20 * P
+    bwd_bytes = 20 * P + (236 + 48 + 40 + 236) * N
+    fp32 = 148 * 128 * 2 * pk["sm_max_mhz"] * 1e6
+    hbm = pk["hbm_gbs"] * 1e9
+    fwd_floor = fwd_bytes / hbm + 14.0 * work["sum_n_contrib"] / fp32
+    out = {"work": work, "fwd_roofline_ms": 1e3 * fwd_floor,
+           "fwd_roofline_frac": 1e3 * fwd_floor / fwd_ms}
+    if bwd_ms is not None:
+        bwd_floor = bwd_bytes / hbm + 40.0 * work["sum_n_contrib"] / fp32
+        out.update({"bwd_roofline_ms": 1e3 * bwd_floor, "bwd_roofline_frac": 1e3 * bwd_floor / bwd_ms})
+    out["roofline_model"] = ("HBM-bound stages at their algorithmic bytes / measured HBM peak plus "
+                             "the blends' FP32 work (sum of n_contrib tested pairs) / derived FP32 "
+                             "peak, serialised; frac = that floor / the measured time")
+    return out
+
+
+def six_op_times(mod, dev, reps: int = 7) -> dict:
+    """CUDA-event medians (ms) of the reference API's six ops, chained as its wrapper chains
+    them, on config 2 (1M clustered Gaussians, 1920x1080) through module `mod` (this library's
+    custom_rasterizer_cuda, or the reference's own extension)."""
+    from gs3d_b200 import scenes
+
+    sc = scenes.config2(0)
+    view = sc.views[0]
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    R, t = view.R.to(dev).contiguous(), view.T.to(dev).contiguous()
+    cam = (-(R.T @ t)).contiguous()
+    op = torch.sigmoid(al).contiguous()
+    H, W = view.height, view.width
+    g = torch.rand(H, W, 3, generator=torch.Generator().manual_seed(5)).to(dev)
+    names = ("project", "SH", "rasterize", "backwards_rasterization", "backwards_SH",
+             "backwards_projection")
+    times = {k: [] for k in names}
+    for k in range(reps + 2):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        ev[0].record()
+        m2, c2, d = mod.project(sc.N, mu, q, s, R, t, view.fx, view.fy, view.cx, view.cy)
+        ev[1].record()
+        col = mod.SH(sc.N, cam, mu, A, kj)
+        ev[2].record()
+        img, ids, ranges, fT, nc = mod.rasterize(sc.N, d, m2, c2, col, op, H, W)
+        ev[3].record()
+        gm, gc, gcol, ga = mod.backwards_rasterization(g, m2, c2, col, op, ids, ranges, fT, nc,
+                                                       sc.N, H, W)
+        ev[4].record()
+        mod.backwards_SH(gcol, mu, A, kj, cam)
+        ev[5].record()
+        mod.backwards_projection(gm, gc, mu, q, s, R, t, view.fx, view.fy, view.cx, view.cy)
+        ev[6].record()
+        torch.cuda.synchronize()
+        if k >= 2:
+            for i, name in enumerate(names):
+                times[name].append(ev[i].elapsed_time(ev[i + 1]))
+    out = {k: statistics.median(v) for k, v in times.items()}
+    out["fwd_ms"] = out["project"] + out["SH"] + out["rasterize"]
+    out["bwd_ms"] = out["backwards_rasterization"] + out["backwards_SH"] + out["backwards_projection"]
+    out["workload"] = "config2: 1M clustered Gaussians, 1920x1080, the six ops chained"
+    return out
+
+
+def reference_extension_b200(dev) -> dict:
+    """The reference's own CUDA extension (all six ops: csrc/bindings.cpp built unmodified by
+    oracle/build_ref.py, projection/SH against the GLM stand-in, "ref+shim") timed on this
+    GPU at config 2, as north_star asks beside every number."""
+    path = str(ROOT / "oracle" / "_ref" / "ref_full")
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    try:
+        import ref_full
+    except ImportError as e:
+        return {"unavailable": f"reference extension not built (oracle/build_ref.py): {e}"}
+    out = six_op_times(ref_full, dev)
+    out["build"] = ("ref+shim: the reference's bindings.cpp and six .cu files unmodified, sm_100a, "
+                    "GLM API stand-in oracle/glm_shim")
     return out
 
 
@@ -386,10 +512,13 @@ NCU_DRAM_BYTES = {
 NCU_WARP_INST = {"blend_forward": 289.6e6, "blend_backward": 551.6e6}
 
 
-def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int) -> dict:
-    """Roofline of the dominant stage over the timed region. The blends are FP32-issue bound
-    (no dense contraction anywhere on the path); the per-Gaussian stages are HBM bound."""
-    name = max((k for k in stage_ms if stage_ms[k] is not None), key=lambda k: stage_ms[k])
+def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int,
+                   name: str | None = None) -> dict:
+    """Roofline of one stage (default: the dominant one) over the timed region. The blends are
+    FP32-issue bound (no dense contraction anywhere on the path); the per-Gaussian stages are
+    HBM bound."""
+    if name is None:
+        name = max((k for k in stage_ms if stage_ms[k] is not None), key=lambda k: stage_ms[k])
     ms = stage_ms[name]
     mean_replayed = statistics.mean(stats["replayed_pairs"])
     mean_pairs = statistics.mean(stats["pairs"])
@@ -488,6 +617,10 @@ def run_reference(args, rank, world):
                              "sample": res["sample"]},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    if torch.cuda.is_available():
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        line["reference_extension_b200"] = reference_extension_b200(dev)
     emit(line)
 
 
@@ -522,6 +655,10 @@ def main() -> int:
     ap.add_argument("--view-throughput", action="store_true",
                     help="with --view-only: the training step's kernel variants (tight bins, "
                          "GS_RENDER_CONCURRENT blend kernels) instead of the single-view ones")
+    ap.add_argument("--six-op", action="store_true",
+                    help="the reference API's six ops on one config-2 view per step (single "
+                         "GPU), through this library; a small fixed workload for profiler "
+                         "captures of the six-op kernels")
     ap.add_argument("--table-only", action="store_true",
                     help="only the per-scene forward/backward/FPS table (single GPU)")
     ap.add_argument("--table-scenes", default=None,
@@ -529,6 +666,13 @@ def main() -> int:
     args = ap.parse_args()
     if args.view_only:
         return run_view(args)
+    if args.six_op:
+        import custom_rasterizer_cuda as crc
+
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        emit({"mode": "six_op", "six_op_config2": six_op_times(crc, dev, reps=args.steps)})
+        return 0
     if args.table_only:
         torch.cuda.set_device(0)
         only = set(args.table_scenes.split(",")) if args.table_scenes else None
@@ -721,7 +865,11 @@ def run_ours(args, rank, world, local) -> int:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d_bytes * world,
                 "d2h_bytes_per_step": 4 * world},
         "roofline": roofline_entry(stage_ms, stats, args.steps * len(mine), pk, args.gaussians),
+        "roofline_blend_forward": roofline_entry(stage_ms, stats, args.steps * len(mine), pk,
+                                                 args.gaussians, name="blend_forward"),
     }
+    if world == 1:
+        line["six_op_config2"] = six_op_times(crc, dev)
     if world == 1 and not args.no_render_table:
         line["render_table"] = render_table(dev)
     if world == 1 and not args.no_cpu_baseline:
