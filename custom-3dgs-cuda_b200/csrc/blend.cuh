@@ -396,12 +396,15 @@ __device__ __forceinline__ void flush_hit_rows(const float* rows, int n_hits, in
 // pixels share one column, so per pixel only sum(dL/dpower), sum(dL/dpower dy) and
 // sum(dL/dpower dy^2) are kept and the dx factors are applied once per splat.
 //
-// kFusedAccum selects the flush: false converts each tile's dL/dconic to dL/dSigma2 and adds
-// into the four reference-layout gradient arrays (9 scalar atomics, as the reference does);
-// true adds the raw sums into g_accum with vector atomics, 3 float4 per Gaussian:
-//   [0] = (dmean.x, dmean.y, dconic.x, dconic.y), [1] = (dconic.z, dopacity, dcol.r, dcol.g),
-//   [2] = (dcol.b, -, -, -), and the conversion happens once per Gaussian later
-//   (dL/dSigma2 is linear in dL/dconic for a fixed conic, so the sums commute with it).
+// Both flushes convert each tile's dL/dconic to dL/dSigma2 = -V G V with the tile's own sums, as
+// the reference does per (tile, Gaussian) (csrc/backward/rasterize_backward.cu:211-221): the
+// conversion is linear, but for near-singular 2D covariances (needle-like splats) its
+// cancellation error depends on what is summed first, and converting per tile keeps the
+// reference's rounding. kFusedAccum selects the destination: false adds into the four
+// reference-layout gradient arrays (9 scalar atomics, as the reference does); true adds into
+// g_accum with vector atomics, 3 float4 per Gaussian:
+//   [0] = (dmean.x, dmean.y, dSigma2.a, dSigma2.b), [1] = (dSigma2.c, dopacity, dcol.r,
+//   dcol.g), [2] = (dcol.b, -, -, -).
 template <bool kFusedAccum, int kPix>
 __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinBlocks)
     blend_backward_kernel(BlendBwdParams p) {
@@ -594,20 +597,21 @@ __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinB
       const float4 r1 = rec[1][t];
       const float vx = r1.x, vy = r1.y, vz = r1.z;
       const float gmx = vx * acc[0] + vy * acc[1], gmy = vy * acc[0] + vz * acc[1];
-      const float gcx = -0.5f * acc[2], gcy = -acc[3], gcz = -0.5f * acc[4];
+      const float gx = -0.5f * acc[2], gy = 0.5f * -acc[3], gz = -0.5f * acc[4];
+      const float ga = -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz);
+      const float gb = -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz);
+      const float gc = -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz);
       if (kFusedAccum && any && g >= 0 && g < p.N) {
         float4* dst = p.g_accum + 3 * (size_t)g;
-        atomicAdd(dst, make_float4(gmx, gmy, gcx, gcy));
-        atomicAdd(dst + 1, make_float4(gcz, acc[8], acc[5], acc[6]));
+        atomicAdd(dst, make_float4(gmx, gmy, ga, gb));
+        atomicAdd(dst + 1, make_float4(gc, acc[8], acc[5], acc[6]));
         atomicAdd(&dst[2].x, acc[7]);
       } else if (any && g >= 0 && g < p.N) {
         atomicAdd(p.g_mean2d + 2 * g, gmx);
         atomicAdd(p.g_mean2d + 2 * g + 1, gmy);
-        const float gx = gcx, gy = 0.5f * gcy, gz = gcz;
-        atomicAdd(p.g_cov2d + 3 * g, -(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz));
-        atomicAdd(p.g_cov2d + 3 * g + 1,
-                  -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz));
-        atomicAdd(p.g_cov2d + 3 * g + 2, -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz));
+        atomicAdd(p.g_cov2d + 3 * g, ga);
+        atomicAdd(p.g_cov2d + 3 * g + 1, gb);
+        atomicAdd(p.g_cov2d + 3 * g + 2, gc);
         atomicAdd(p.g_colors + 3 * g, acc[5]);
         atomicAdd(p.g_colors + 3 * g + 1, acc[6]);
         atomicAdd(p.g_colors + 3 * g + 2, acc[7]);

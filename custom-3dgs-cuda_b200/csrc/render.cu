@@ -6,9 +6,9 @@
 // Forward: render_preprocess_kernel (projection + SH colour + screen radius + binning prep,
 // one thread per Gaussian, SH rows staged warp-wide) followed by the shared depth sort, pair
 // duplication, tile sort, tile ranges and blend of launch_sort_and_blend.
-// Backward: blend_backward_kernel<true> accumulates raw per-Gaussian sums (mean, conic,
-// opacity, colour gradients) with vector atomics; render_gaussian_backward_kernel then, per
-// Gaussian, converts dL/dconic to dL/dSigma2 once, runs the SH and projection backward and
+// Backward: blend_backward_kernel<true> accumulates per-Gaussian sums (dL/dmean2d, dL/dSigma2
+// converted per tile, opacity and colour gradients) with vector atomics;
+// render_gaussian_backward_kernel then, per Gaussian, runs the SH and projection backward and
 // writes (or accumulates into) the six parameter gradients and dL/dmean2d.
 #include "binning.cuh"
 #include "blend.cuh"
@@ -159,13 +159,7 @@ __global__ void __launch_bounds__(256, 3) render_gaussian_backward_kernel(Gaussi
   }
   float* row = stage + lane * kShRestFloats;
   if (valid && touched) {
-    // dL/dconic -> dL/dSigma2 = -V G V with G's off-diagonal half of the packed sum
-    const float4 r1 = p.records[3 * i + 1];
-    const float vx = r1.x, vy = r1.y, vz = r1.z;
-    const float gx = a0.z, gy = 0.5f * a0.w, gz = a1.x;
-    const float3 gcov = make_float3(-(vx * vx * gx + 2.0f * vx * vy * gy + vy * vy * gz),
-                                    -2.0f * (vx * vy * gx + (vx * vz + vy * vy) * gy + vy * vz * gz),
-                                    -(vy * vy * gx + 2.0f * vy * vz * gy + vz * vz * gz));
+    const float3 gcov = make_float3(a0.z, a0.w, a1.x);  // dL/dSigma2, converted per tile
     const float2 gmean = make_float2(a0.x, a0.y);
     const float3 gcol = make_float3(a1.z, a1.w, a2.x);
     Camera cam;

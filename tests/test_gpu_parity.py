@@ -354,22 +354,57 @@ def _needle_scene(n=40_000, seed=12):
     return scenes.Scene("needles", mu, q, s, alpha, A, kj)
 
 
+def band_stats(a, b, rtol=1e-4):
+    """(elements beyond rtol (|b| + rms(b)), worst error / that band)."""
+    b = np.asarray(b, np.float64)
+    a = np.asarray(a, np.float64).reshape(b.shape)
+    rms = float(np.sqrt(np.mean(b * b))) if b.size else 0.0
+    band = rtol * (np.abs(b) + rms) + 1e-30
+    err = np.abs(a - b)
+    return int((err > band).sum()), float((err / band).max())
+
+
+def assert_like_reference_nondeterminism(a, runs, what, count_factor=8.0, worst_factor=2.0):
+    """`a` against the first of several runs of the reference, which differ from each other
+    only in the order of their float atomics: the elements beyond the 1e-4 band may number at
+    most `count_factor` times, and the worst excess may be at most `worst_factor` times, what
+    the reference's other runs show against that same first run."""
+    ref_out, ref_worst = zip(*(band_stats(r, runs[0]) for r in runs[1:]))
+    out, worst = band_stats(a, runs[0])
+    limit = max(count_factor * max(ref_out), 1e-4 * runs[0].size)
+    assert out <= limit, (f"{what}: {out} elements beyond the 1e-4 band; the reference's own "
+                          f"runs: {list(ref_out)}")
+    assert worst <= worst_factor * max(max(ref_worst), 1.0), (
+        f"{what}: worst {worst:.1f}x the band; the reference's own runs: "
+        f"{[round(w, 1) for w in ref_worst]}")
+
+
 def test_ellipse_cull_matches_reference_kernels_on_needles(crc, cuda_device):
     """The opacity-ellipse cull (every blend variant) skips only splats that fail the opacity
     test: on needle-like faint splats the image, transmittance and contributor counts equal the
-    reference's own kernels bit for bit, the fused path's variants give the same image, the
-    blend backward agrees with the reference's, and every fused backward variant (per-row reach
-    mask at four pixels per thread included) gives the blend-level sums (dL/dmean2d, opacity,
-    SH) of the reference's blend backward. The mean / rotation / scale gradients go through
-    the needles' near-singular 2D covariances, which amplify rounding-order differences (in the
-    two-pixel and four-pixel variants alike: against gradients built from the reference's blend
-    backward both put 2% of the rotation gradients beyond the 1e-4 band), so those are compared
-    between variants at 1e-3 with a 0.1% outlier budget."""
+    reference's own kernels bit for bit, the fused path's variants give the same image, and the
+    blend backward agrees with the reference's within 1e-4.
+
+    The parameter gradients are compared with the gradients built from the reference's blend
+    backward (its dL/dmean2d, dL/dSigma2, colour and opacity sums through the SH and projection
+    backward). The needles' near-singular 2D covariances amplify any rounding difference in
+    dL/dSigma2 through the projection backward so much that the reference does not meet a flat
+    1e-4 bar against itself: two runs of its blend backward, which differ only in the order of
+    their float atomics, put 0.45% of the rotation gradients beyond the 1e-4 band (worst ~200x).
+    So for the mean, rotation and log-scale gradients of every variant, the elements beyond the
+    1e-4 band and the worst excess must be of the order the reference's own runs show (fewer
+    than 8x as many elements, at most 2x the worst excess, against the same run; measured on a
+    B200: 3-5x as many, worst below the reference's own); opacity and SH gradients must be
+    within 1e-4. dL/dSigma2 is converted from dL/dconic per tile in float, as the reference
+    does: converting the same sums in double moved the results further from the reference's
+    (about 5x the count), because the reference's own float rounding of that conversion is a
+    large part of its result for these splats."""
     from custom_rasterizer_cuda.render import render_backward, render_forward
-    from gs3d_b200 import scenes
 
     ref = _ref_module()
     sc = _needle_scene()
+    from gs3d_b200 import scenes
+
     view = scenes.pinhole((0.3, -0.2, 6.0), 517, 291, 420.0)
     out = gpu_forward(crc, sc, view, cuda_device)
     H, W = view.height, view.width
@@ -388,27 +423,29 @@ def test_ellipse_cull_matches_reference_kernels_on_needles(crc, cuda_device):
         assert_grad_close(np32(a), np32(b), what + " (needles)")
     mu, q, s, al, A, kj = to_dev(sc, cuda_device)
     cam = out["cam"].reshape(3)
-    r_A, r_kj, _ = crc.backwards_SH(r_blend[2], mu, A, kj, cam)
-    blend_level = {"opacity": r_blend[3].reshape(-1), "A": r_A, "kj": r_kj,
-                   "mean2d": r_blend[0]}
+
+    def chained(blend):
+        gA, gkj, gmu_sh = crc.backwards_SH(blend[2], mu, A, kj, cam)
+        gmu, gq, gs = crc.backwards_projection(blend[0], blend[1], mu, q, s, out["R"], out["t"],
+                                               view.fx, view.fy, view.cx, view.cy)
+        return {"mu": np32(gmu_sh + gmu), "q": np32(gq), "s": np32(gs),
+                "opacity": np32(blend[3].reshape(-1)), "A": np32(gA), "kj": np32(gkj),
+                "mean2d": np32(blend[0])}
+
+    runs = [chained(r_blend)] + [chained(ref.backwards_rasterization(*args)) for _ in range(3)]
     op = torch.sigmoid(al).reshape(-1).contiguous()
-    grads = {}
+    names = ("mu", "q", "s", "opacity", "A", "kj", "mean2d")
     for tight, concurrent in ((False, False), (False, True), (True, True)):
         img, _, st = render_forward(mu, q, s, op, A, kj, out["R"], out["t"], out["cam"].reshape(3),
                                     view.fx, view.fy, view.cx, view.cy, H, W, tight_bins=tight,
                                     concurrent=concurrent)
         assert torch.equal(img, r_img), (tight, concurrent)
         assert torch.equal(st.final_T, r_T), (tight, concurrent)
-        grads[(tight, concurrent)] = render_backward(st, g, mu, q, s, A, kj, out["R"], out["t"],
-                                                     out["cam"].reshape(3), view.fx, view.fy,
-                                                     view.cx, view.cy)
-    names = ("mu", "q", "s", "opacity", "A", "kj", "mean2d")
-    base = grads[(False, False)]
-    for key, gr in grads.items():
+        gr = render_backward(st, g, mu, q, s, A, kj, out["R"], out["t"], out["cam"].reshape(3),
+                             view.fx, view.fy, view.cx, view.cy)
         for a, what in zip(gr, names):
-            if what in blend_level:
-                assert_grad_close(np32(a), np32(blend_level[what]), f"{what} {key}")
-        if key != (False, False):
-            for a, b, what in zip(gr[:3], base[:3], names[:3]):
-                assert_grad_close(np32(a), np32(b), f"{what} {key}", rtol=1e-3,
-                                  outlier_frac=1e-3)
+            key = f"{what} {(tight, concurrent)}"
+            if what in ("mu", "q", "s"):
+                assert_like_reference_nondeterminism(np32(a), [r[what] for r in runs], key)
+            else:
+                assert_grad_close(np32(a), runs[0][what], key)
