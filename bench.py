@@ -558,22 +558,32 @@ def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n:
 
 
 # ---- CPU baseline (the oracle) ----------------------------------------------------------------
-def cpu_baseline_sample(scene, view, target) -> dict:
-    """One view's forward + backward on the host cores through the CPU oracle."""
+def cpu_baseline_sample(scene, view, target, adam_seconds: float | None = None) -> dict:
+    """One view of the training step on the host cores: the CPU oracle's forward and backward
+    (projection, SH, binning + stable sort, blend, blend / SH / projection backward) with the
+    step's loss (0.8 L1 + 0.2 (1 - SSIM), its torch formulation on the CPU, whose autograd gives
+    the image gradient) and one eighth of a CPU Adam step over all parameters (the step's
+    optimizer work per view; `adam_seconds` from `cpu_adam_seconds`)."""
     import numpy as np
 
+    from gs3d_b200.train_step import gaussian_window, reconstruction_loss
     from oracle import oracle as O
 
     O.build()
     threads = O.max_threads()
     O.set_threads(threads)
+    torch.set_num_threads(threads)
     R, t = view.R.numpy(), view.T.numpy()
     op = torch.sigmoid(scene.alpha).numpy().reshape(-1)
+    window = gaussian_window()
     t0 = time.perf_counter()
     out = O.render(scene.mu.numpy(), scene.q.numpy(), scene.s.numpy(), op, scene.A.numpy(),
                    scene.k_j.numpy(), R, t, view.fx, view.fy, view.cx, view.cy, view.height,
                    view.width)
-    gimg = np.sign(out["img"] - target.numpy()).astype(np.float32) / out["img"].size
+    img = torch.from_numpy(out["img"]).requires_grad_(True)
+    loss = reconstruction_loss(img, target, window)
+    loss.backward()
+    gimg = img.grad.numpy().astype(np.float32)
     gm, gc, gcol, ga, _ = O.rasterize_backward(gimg, out["mean2d"], out["cov2d"], out["colors"],
                                                op, out["sorted_ids"], out["tile_ranges"],
                                                out["final_T"], out["n_contrib"], view.height,
@@ -583,11 +593,30 @@ def cpu_baseline_sample(scene, view, target) -> dict:
     O.project_backward(gm, gc, scene.mu.numpy(), scene.q.numpy(), scene.s.numpy(), R, t,
                        view.fx, view.fy, view.cx, view.cy)
     dt = time.perf_counter() - t0
+    if adam_seconds is not None:
+        dt += adam_seconds / BATCH_VIEWS
     return {"value": 1.0 / dt, "unit": UNIT, "cores": threads, "kind": "port",
             "seconds": dt,
             "sample": "one 1920x1080 view of the 1M-Gaussian config-4 batch: projection, SH, "
-                      "binning + stable 64-bit sort, blend, blend/SH/projection backward "
-                      "(L1 gradient; the SSIM term and Adam are not in the CPU sample)"}
+                      "binning + stable 64-bit sort, blend, the L1 + SSIM loss and its image "
+                      "gradient, blend/SH/projection backward, and 1/8 of an Adam step over "
+                      "all parameters (the step's optimizer work per view)"}
+
+
+def cpu_adam_seconds(scene) -> float:
+    """Seconds of one torch.optim.Adam step (eps 1e-15, the step's learning rates) over all
+    parameters on the host cores."""
+    from gs3d_b200.train_step import LEARNING_RATES, PARAM_NAMES
+
+    params = [p.detach().clone().requires_grad_(True) for p in scene.params()]
+    for p in params:
+        p.grad = torch.randn_like(p) * 1e-3
+    opt = torch.optim.Adam([{"params": [p], "lr": LEARNING_RATES[n]}
+                            for p, n in zip(params, PARAM_NAMES)], eps=1e-15)
+    opt.step()  # state allocation outside the timing
+    t0 = time.perf_counter()
+    opt.step()
+    return time.perf_counter() - t0
 
 
 # ---- main -------------------------------------------------------------------------------------
@@ -599,12 +628,14 @@ def run_reference(args, rank, world):
     from gs3d_b200 import scenes
 
     sc, targets = scenes.config4(0, n=N_GAUSSIANS, n_views=BATCH_VIEWS)
+    adam_s = cpu_adam_seconds(sc)
     for _ in range(args.warmup_ref):
-        cpu_baseline_sample(sc, sc.views[0], targets[0])
+        cpu_baseline_sample(sc, sc.views[0], targets[0], adam_s)
     secs = []
     res = None
     for k in range(args.steps):
-        res = cpu_baseline_sample(sc, sc.views[k % BATCH_VIEWS], targets[k % BATCH_VIEWS])
+        res = cpu_baseline_sample(sc, sc.views[k % BATCH_VIEWS], targets[k % BATCH_VIEWS],
+                                  adam_s)
         secs.append(res["seconds"])
     total = sum(secs)
     value = args.steps / total
@@ -873,7 +904,8 @@ def run_ours(args, rank, world, local) -> int:
     if world == 1 and not args.no_render_table:
         line["render_table"] = render_table(dev)
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_sample(sc, sc.views[0], targets[0])
+        line["cpu_baseline"] = cpu_baseline_sample(sc, sc.views[0], targets[0],
+                                                   cpu_adam_seconds(sc))
         line["cpu_baseline"].pop("seconds", None)
     emit(line)
     return 0
