@@ -151,7 +151,7 @@ __device__ __forceinline__ unsigned warp_block_rows(float4 r0, float4 r1, float 
 }
 
 struct BlendFwdParams {
-  int W, H, tiles_x;
+  int W, H, tiles_x, num_tiles;
   const int2* ranges;
   const int* tile_order;  // CTA -> tile (tile_order_kernel); null: raster order
   const int* sorted_ids;
@@ -177,6 +177,10 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
   __shared__ float4 s_rec[2][3][kBlendBatch];
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
+  if (tile < 0 || tile >= p.num_tiles) {  // never for a tile order the sort wrote
+    if (threadIdx.x == 0) raise_device_error(kErrBadIndex);
+    return;
+  }
   const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
   const int tid = threadIdx.x, lane = tid & 31;
   const BlendGeometry<kPix> geo(tile_x, tile_y);
@@ -282,6 +286,12 @@ static __global__ void __launch_bounds__(kTilePixels / kPix)
 
 struct BlendBwdParams {
   int N, W, H, tiles_x;
+  int num_tiles;
+  // the forward's pair count and capacity (fused path): a forward whose pairs overflowed its
+  // buffers wrote no tile order, ranges or counts, so its backward does nothing; null: the
+  // caller's tile ranges are valid (stand-alone API)
+  const int* pair_count;
+  long long pair_capacity;
   const float* grad_img;
   const int2* ranges;
   const int* tile_order;  // CTA -> tile (tile_order_kernel); null: raster order
@@ -417,7 +427,12 @@ __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinB
   __shared__ __align__(16) float s_red[kRowReduce ? kThreads / 32 : 1][kRowReduce ? kRedHits * 9 * 32 : 4];
   float* const my_rows = s_red[kRowReduce ? (threadIdx.x >> 5) : 0];
   int pending = 0, pend_k0 = 0;
+  if (p.pair_count && (long long)(*p.pair_count) > p.pair_capacity) return;
   const int tile = p.tile_order ? p.tile_order[blockIdx.x] : (int)blockIdx.x;
+  if (tile < 0 || tile >= p.num_tiles) {  // never for a tile order the forward wrote
+    if (threadIdx.x == 0) raise_device_error(kErrBadIndex);
+    return;
+  }
   const int tile_x = tile % p.tiles_x, tile_y = tile / p.tiles_x;
   const int tid = threadIdx.x, lane = tid & 31;
   const BlendGeometry<kPix> geo(tile_x, tile_y);
@@ -532,10 +547,12 @@ __global__ void __launch_bounds__(kTilePixels / kPix, BlendBwdShape<kPix>::kMinB
           if (alpha < (1.0f / 255.0f)) continue;
           active = true;
           const float4 r2 = rec[2][k];
+          // the reference divides by max(1 - alpha, 1e-4); alpha <= 0.99 keeps 1 - alpha >= 0.01,
+          // so the clamp never acts and is left out. Approximate division (2 ulp): the
+          // recovered T drifts by a few 1e-6 over a pixel's replay, far inside the gradient
+          // tolerance
           const float one_minus = 1.0f - alpha;
-          // approximate division (2 ulp): the recovered T drifts by a few 1e-6 over a
-          // pixel's replay, far inside the gradient tolerance
-          const float T_before = __fdividef(T[q], fmaxf(one_minus, 1e-4f));
+          const float T_before = __fdividef(T[q], one_minus);
           const float wgt = alpha * T_before;
           v[5] += wgt * gr[q];
           v[6] += wgt * gg[q];

@@ -167,14 +167,31 @@ __device__ __forceinline__ unsigned wait_status(const unsigned* p) {
 }
 
 // Single-thread look-back: exclusive prefix of `tile` from the status words of its
-// predecessors (status[0..tile-1]); each status word is strided by `stride` words.
+// predecessors (status[0..tile-1]); each status word is strided by `stride` words. The
+// predecessors are read kLookbackBatch at a time (independent loads in flight together), then
+// consumed nearest first until one carries an inclusive prefix: when every tile of a pass runs
+// at once, a tile's walk back to the nearest prefix is long, and one dependent L2 round trip per
+// predecessor made the walk, not the data, set the pass's time.
+constexpr int kLookbackBatch = 8;
+
 __device__ __forceinline__ unsigned lookback_serial(const unsigned* status, int tile,
                                                     int stride) {
   unsigned excl = 0;
-  for (int p = tile - 1; p >= 0; --p) {
-    unsigned v = wait_status(status + (size_t)p * stride);
-    excl += v & kValueMask;
-    if (v & kFlagPrefix) break;
+  for (int base = tile - 1; base >= 0; base -= kLookbackBatch) {
+    unsigned v[kLookbackBatch];
+#pragma unroll
+    for (int k = 0; k < kLookbackBatch; ++k)
+      v[k] = base - k >= 0 ? ld_relaxed(status + (size_t)(base - k) * stride) : kFlagPrefix;
+    bool done = false;
+#pragma unroll
+    for (int k = 0; k < kLookbackBatch; ++k) {
+      if (done) continue;
+      unsigned w = v[k];
+      if ((w & kFlagMask) == 0u) w = wait_status(status + (size_t)(base - k) * stride);
+      excl += w & kValueMask;
+      done = (w & kFlagPrefix) != 0u;
+    }
+    if (done) break;
   }
   return excl;
 }

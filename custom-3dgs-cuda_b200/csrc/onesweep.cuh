@@ -12,7 +12,10 @@ namespace gs {
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 12;                          // items per thread
+#ifndef GS_SORT_ITEMS
+#define GS_SORT_ITEMS 12
+#endif
+constexpr int kSortItems = GS_SORT_ITEMS;               // items per thread
 constexpr int kSortTileItems = kSortThreads * kSortItems;  // 3072 items per tile
 constexpr int kRadix = 256;
 

@@ -151,7 +151,7 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
       SortPass sp;
       sp.keys_in = dk[pass & 1];
       sp.vals_in = dv[pass & 1];
-      sp.keys_out = dk[(pass + 1) & 1];
+      sp.keys_out = pass < 3 ? dk[(pass + 1) & 1] : nullptr;  // the duplication reads ids only
       sp.vals_out = dv[(pass + 1) & 1];
       sp.n_items = &hdr->n_visible;
       sp.overflow_count = &hdr->pair_count;
@@ -223,6 +223,7 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
   fp.W = W;
   fp.H = H;
   fp.tiles_x = L.tiles_x;
+  fp.num_tiles = (int)L.T;
   fp.ranges = reinterpret_cast<const int2*>(tile_ranges);
   fp.tile_order = tile_order;
   fp.sorted_ids = sorted_ids;
@@ -339,6 +340,9 @@ extern "C" int gs_rasterize_backward(int N, int H, int W, const float* grad_img,
   bp.W = W;
   bp.H = H;
   bp.tiles_x = tiles_x;
+  bp.num_tiles = tiles_x * tiles_y;
+  bp.pair_count = nullptr;  // the caller's tile ranges are valid
+  bp.pair_capacity = 0;
   bp.grad_img = grad_img;
   bp.ranges = reinterpret_cast<const int2*>(tile_ranges);
   bp.tile_order = nullptr;  // raster order: this entry point has no forward workspace

@@ -340,6 +340,10 @@ extern "C" int gs_render_backward(int N, int H, int W, const float* grad_img, co
   bp.W = W;
   bp.H = H;
   bp.tiles_x = L.tiles_x;
+  bp.num_tiles = (int)L.T;
+  bp.pair_count = &reinterpret_cast<const RasterHeader*>(
+                       static_cast<const char*>(fwd_workspace) + L.header)->pair_count;
+  bp.pair_capacity = pair_capacity;
   bp.grad_img = grad_img;
   bp.ranges = reinterpret_cast<const int2*>(tile_ranges);
   bp.tile_order =

@@ -13,8 +13,14 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _MAX_PAIRS, _capacity, _m_event, _ptr, _stream, _tiles
+from . import _MAX_PAIRS, _capacity, _ptr, _stream, _tiles
 from ._lib import check, lib
+
+
+# Scenes whose worst case of (tile, Gaussian) pairs -- every Gaussian in every tile, N * T --
+# stays within this many pairs get pair buffers for that worst case (16 bytes per pair of
+# workspace), so no call can overflow and the host never waits for the pair count.
+_WORST_CASE_PAIRS = 1 << 22
 
 
 @dataclass
@@ -22,22 +28,46 @@ class RenderState:
     workspace: torch.Tensor
     capacity: int
     sorted_ids: torch.Tensor   # [capacity]; the first M are valid
-    pairs: int                 # M
     tile_ranges: torch.Tensor
     final_T: torch.Tensor
     n_contrib: torch.Tensor
     height: int
     width: int
     backward_flags: int = 0    # GS_RENDER_CONCURRENT when the forward was given it
+    m_host: torch.Tensor | None = None  # pinned int32: M, valid once m_event has completed
+    m_event: object = None
+    _pairs: int | None = None
+    _key: tuple | None = None
+
+    @property
+    def pairs(self) -> int:
+        """M, the number of (tile, Gaussian) pairs (waits for it on first use)."""
+        if self._pairs is None:
+            self.m_event.synchronize()
+            self._pairs = int(self.m_host[0])
+            _capacity.update(*self._key, self._pairs)
+        return self._pairs
+
+    def overflowed(self) -> bool:
+        """True if M exceeded the pair buffers: the image and the state are then unusable and
+        the view must be rendered again (waits for M on first use)."""
+        return self.pairs > self.capacity
 
 
 def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy, height,
-                   width, tight_bins: bool = False, concurrent: bool = False):
+                   width, tight_bins: bool = False, concurrent: bool = False,
+                   defer_check: bool = False, capacity: int | None = None):
     """(img[H,W,3], radii[N], RenderState). `opacity` is post-sigmoid, N or [N,1].
     tight_bins: bin splats only into tiles where they can pass the opacity test (same image
     and gradients, shorter tile lists; the state's lists then differ from the reference's).
     concurrent: the caller overlaps several views on streams; the blend kernels (this one and
-    the state's backward) use their throughput variants (GS_RENDER_CONCURRENT)."""
+    the state's backward) use their throughput variants (GS_RENDER_CONCURRENT).
+    Pair buffers are sized for the scene's worst case when that is small (no host wait at
+    all), otherwise from the pair count of earlier calls (+12.5%) or `capacity`. Then, by
+    default, the call waits for the pair count and renders again with exactly M if the guess
+    was short; with defer_check=True it returns at once and the caller must ask
+    `state.overflowed()` before using the image or the state, and render again (with
+    capacity=state.pairs) if it is true."""
     N, H, W = int(mu.shape[0]), int(height), int(width)
     dev = mu.device
     T = _tiles(H, W)
@@ -50,12 +80,18 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
     radii = torch.empty((N,), **f32)
     mode = 1 if tight_bins else 0
     flags = mode | (2 if concurrent else 0)
-    cap = _capacity.guess(N, H, W, mode)
+    worst = N * T
+    safe = worst <= _WORST_CASE_PAIRS
+    if capacity is not None:
+        cap = int(capacity)
+    else:
+        cap = worst if safe else _capacity.guess(N, H, W, mode)
+    key = (N, H, W, mode)
     with torch.cuda.device(dev):
         stream = _stream(dev)
-        m_host = torch.empty((1,), dtype=torch.int32, pin_memory=True)
-        ev = _m_event()
+        slots = _pair_count_slot()
         for _attempt in range(2):
+            slot, m_host, ev = slots.take()
             ws_bytes = lib.gs_render_workspace_size(N, H, W, cap)
             ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8)
             sorted_ids = torch.empty((max(cap, 1),), **i32)
@@ -65,19 +101,65 @@ def render_forward(mu, q, s, opacity, albedo, k_j, R, t, cam_pos, fx, fy, cx, cy
                 ws.data_ptr(), ws_bytes, cap, _ptr(img), sorted_ids.data_ptr(),
                 _ptr(tile_ranges), _ptr(final_T), _ptr(n_contrib), _ptr(radii),
                 m_host.data_ptr(), ev.handle, flags, stream))
-            ev.synchronize()
-            M = int(m_host[0])
-            _capacity.update(N, H, W, M, mode)
-            if M <= cap:
-                state = RenderState(ws, cap, sorted_ids, M, tile_ranges, final_T, n_contrib, H, W,
-                                    flags & 2)
+            state = RenderState(ws, cap, sorted_ids, tile_ranges, final_T, n_contrib, H, W,
+                                flags & 2, m_host, ev, None, key)
+            slots.own(slot, state)
+            if safe or defer_check or not state.overflowed():
                 return img, radii, state
+            M = state.pairs
             if M > _MAX_PAIRS:
                 raise RuntimeError(
                     f"render: {M} (tile, Gaussian) pairs exceed the supported maximum of "
                     f"{_MAX_PAIRS}; reduce the number of Gaussians or the image size")
             cap = M
     raise RuntimeError("pair count kept growing between attempts")
+
+
+class _PairCountSlots:
+    """Pinned host words that receive each render's pair count, with an event per word. A word
+    is reused round-robin; before that, the render that used it last is made to read its count
+    (its copy long finished by then), so a state never sees another render's count and no
+    copy ever lands in memory that has been handed to someone else."""
+
+    def __init__(self, n: int = 256) -> None:
+        import threading
+        import weakref
+
+        self._weakref = weakref.ref
+        self.buf = torch.empty((n,), dtype=torch.int32, pin_memory=True)
+        self.events: list = [None] * n
+        self.owners: list = [None] * n
+        self.next = 0
+        self.lock = threading.Lock()
+
+    def take(self):
+        from ._lib import Event
+
+        with self.lock:
+            k = self.next
+            self.next = (k + 1) % self.buf.numel()
+            owner = self.owners[k]() if self.owners[k] is not None else None
+            if owner is not None:
+                owner.pairs  # resolves its count before the word is reused
+            ev = self.events[k]
+            if ev is None:
+                ev = self.events[k] = Event()
+            else:
+                ev.synchronize()
+            return k, self.buf[k:k + 1], ev
+
+    def own(self, k: int, state) -> None:
+        self.owners[k] = self._weakref(state)
+
+
+_slots = None
+
+
+def _pair_count_slot():
+    global _slots
+    if _slots is None:
+        _slots = _PairCountSlots()
+    return _slots
 
 
 def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, cam_pos, fx, fy,

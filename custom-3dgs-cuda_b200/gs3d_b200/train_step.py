@@ -316,35 +316,54 @@ class Trainer:
             for st in streams:
                 if st is not main:
                     st.wait_stream(main)
-            losses, prev_done = [], None
-            for k, vi in enumerate(views):
+            # The host does not wait for any view's pair count here: each view's pair buffers
+            # are sized from the last pair count seen (+12.5%), and all views are checked once
+            # below, before the update. A view whose pairs overflowed its buffers rendered
+            # nothing (its blend kernels and backward do no work, adding zero gradients) and is
+            # rendered again with exact buffers.
+            def render_view(k, vi, st, done, prev_done, capacity=None, accumulate=None):
                 v = self.views[vi]
                 cam = self.cam_positions[vi]
-                if before_view is not None:
-                    before_view(vi)
-                st = streams[k % len(streams)]
-                done = self._accum_events[k % 2] if len(streams) > 1 else None
                 with torch.cuda.stream(st):
                     img, _, rs = render_forward(mu, q, s, opacity, A, kj, v["R"], v["T"], cam,
                                                 v["fx"], v["fy"], v["cx"], v["cy"], v["height"],
                                                 v["width"], tight_bins=self.tight_bins,
-                                                concurrent=self.concurrent_views)
+                                                concurrent=self.concurrent_views,
+                                                defer_check=True, capacity=capacity)
                     target = targets.get(vi) if staged else targets[vi]
                     loss, gimg = l1_ssim_value_and_grad(img, target, LAMBDA_DSSIM)
-                    if staged:
+                    if staged:  # the next step's copy into this target waits for this point
                         targets.release(vi)
                     render_backward(rs, gimg, mu, q, s, A, kj, v["R"], v["T"], cam, v["fx"],
                                     v["fy"], v["cx"], v["cy"], want_mean2d_grad=False, out=out,
                                     stats=(fg.grad_norm_sum, fg.grad_count, fg.max_grad,
                                            v["width"] / 2.0, v["height"] / 2.0),
-                                    accum_wait=prev_done, accum_done=done, accumulate=k > 0)
+                                    accum_wait=prev_done, accum_done=done,
+                                    accumulate=(k > 0) if accumulate is None else accumulate)
+                return loss, rs
+
+            losses, states, prev_done = [], [], None
+            for k, vi in enumerate(views):
+                if before_view is not None:
+                    before_view(vi)
+                st = streams[k % len(streams)]
+                done = self._accum_events[k % 2] if len(streams) > 1 else None
+                loss, rs = render_view(k, vi, st, done, prev_done)
                 prev_done = done
                 if st is not main:
                     loss.record_stream(main)
                 losses.append(loss)
+                states.append(rs)
             for st in streams:
                 if st is not main:
                     main.wait_stream(st)
+            for k, (vi, rs) in enumerate(zip(views, states)):
+                if rs.overflowed():
+                    loss, rs2 = render_view(k, vi, main, None, None, capacity=rs.pairs,
+                                            accumulate=True)
+                    if rs2.overflowed():
+                        raise RuntimeError("pair count changed between two renders of a view")
+                    losses[k] = loss
             total = torch.stack(losses).sum() if losses else torch.zeros((), device=self.device)
             # d loss / d logit = d loss / d opacity * sigmoid'(logit), once per step
             g.alpha.grad.view(-1).addcmul_(self.g_opacity, opacity * (1.0 - opacity))

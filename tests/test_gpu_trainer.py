@@ -93,3 +93,32 @@ def test_concurrent_view_streams_give_the_same_bucket(cuda_device):
     assert got[1][0] == got[2][0]
     assert_grad_close(got[2][1].numpy(), got[1][1].numpy(), "bucket")
     assert_grad_close(got[2][2].numpy(), got[1][2].numpy(), "max statistic")
+
+
+def test_direct_step_renders_overflowed_views_again(cuda_device):
+    """The direct step does not wait for each view's pair count: buffers are sized from the
+    last count seen and every view is checked once before the update. With the remembered count
+    forced far below the real one, every view overflows, is rendered again with exact buffers,
+    and the step's loss and bucket equal those of a step whose guesses were right."""
+    import custom_rasterizer_cuda as crc
+    from gs3d_b200.train_step import Trainer
+
+    sc, views, targets = _small_setup()
+    tg = [t.to(cuda_device) for t in targets]
+    got = {}
+    for forced in (False, True):
+        tr = Trainer(sc, views, tg, cuda_device, view_streams=1)
+        tr.opt.step = lambda: None
+        tr.step()  # warm-up: the pair counts of these views are remembered
+        tr.fg.zero()
+        if forced:
+            for v in views:
+                crc._capacity.update(sc.N, v.height, v.width, 10, 1 if tr.tight_bins else 0)
+        loss = tr.step()
+        torch.cuda.synchronize()
+        got[forced] = (float(loss), tr.fg.buffer.cpu().numpy().copy(),
+                       tr.fg.max_grad.cpu().numpy().copy())
+    assert got[True][0] == got[False][0]
+    assert_grad_close(got[True][1], got[False][1], "bucket")
+    assert_grad_close(got[True][2], got[False][2], "max statistic")
+    assert crc.device_error_bits() == 0
