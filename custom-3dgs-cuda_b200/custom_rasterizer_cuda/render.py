@@ -45,7 +45,8 @@ class RenderState:
         if self._pairs is None:
             self.m_event.synchronize()
             self._pairs = int(self.m_host[0])
-            _capacity.update(*self._key, self._pairs)
+            n, h, w, mode = self._key
+            _capacity.update(n, h, w, self._pairs, mode)
         return self._pairs
 
     def overflowed(self) -> bool:

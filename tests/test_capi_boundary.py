@@ -148,3 +148,13 @@ def test_training_entry_points_reject_bad_arguments_before_cuda():
                                 *([256] * 4), 256, 1 << 20, *([256] * 7), 0, None, None, None,
                                 1.0, 1.0, None, None, 1, None) == _lib.GS_ERR_INVALID_ARG
     assert b"flag" in L.gs_last_error()
+
+
+def test_pair_capacity_memory_uses_the_last_count():
+    """The pair-buffer guess for a (N, H, W, binning mode) is the last pair count seen + 12.5%
+    + 4096, and counts of one binning mode do not leak into the other."""
+    from custom_rasterizer_cuda import _capacity
+
+    _capacity.update(123, 45, 67, 10_000, 1)
+    assert _capacity.guess(123, 45, 67, 1) == 10_000 + 10_000 // 8 + 4096
+    assert _capacity.guess(123, 45, 67, 0) == 8 * 123 + 4096

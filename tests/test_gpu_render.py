@@ -119,3 +119,30 @@ def test_tight_bins_keep_image_and_gradients(crc, cuda_device, case):
     assert st1.pairs <= st0.pairs
     for a, b, what in zip(g1, g0, ("mu", "q", "s", "opacity", "A", "kj", "mean2d")):
         assert_grad_close(np32(a), np32(b), what + " (tight bins)")
+
+
+def test_pair_buffers_sized_from_the_last_count(cuda_device):
+    """A second render of a view gets pair buffers of the first one's count + 12.5% + 4096 (one
+    attempt, no re-render); a scene whose worst case (N x tiles) is small gets buffers for that
+    worst case and never waits for its count."""
+    from custom_rasterizer_cuda.render import render_forward
+    from gs3d_b200 import scenes
+
+    def render(sc, view):
+        mu, q, s, al, A, kj = (p.to(cuda_device).contiguous() for p in sc.params())
+        R, t = view.R.to(cuda_device), view.T.to(cuda_device)
+        cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+        op = torch.sigmoid(al).reshape(-1).contiguous()
+        return render_forward(mu, q, s, op, A, kj, R, t, cam, view.fx, view.fy, view.cx,
+                              view.cy, view.height, view.width)
+
+    sc = scenes.config2(11, n=50_000)
+    view = scenes.pinhole((0.0, 0.0, 8.0), 480, 270, 375.0)
+    _, _, st1 = render(sc, view)
+    _, _, st2 = render(sc, view)
+    m = st1.pairs
+    assert st2.capacity == m + m // 8 + 4096 and st2.pairs == m
+    sc0 = scenes.config0(0)
+    _, _, st0 = render(sc0, sc0.views[0])
+    tiles = ((sc0.views[0].width + 15) // 16) * ((sc0.views[0].height + 15) // 16)
+    assert st0.capacity == sc0.N * tiles and st0.pairs <= st0.capacity
