@@ -497,19 +497,17 @@ def view_pair_stats(trainer, views: list[dict]) -> dict:
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each stage's kernel,
-# from one `ncu --set full --clock-control none` capture of a config-2 view (1M Gaussians of
-# the config-4 distribution at 1920x1080) with the training step's kernels:
-# `bench.py --view-only --view-throughput --steps 1 --warmup 1` (the blend backward's figures
-# from a later capture of the same command with `--metrics`, after its shared-memory
-# reduction change).
+# from one `ncu --clock-control none` capture per kernel (one launch each) of a config-2 view
+# (1M Gaussians of the config-4 distribution at 1920x1080) with the training step's kernels:
+# `bench.py --view-only --view-throughput --steps 1 --warmup 1` (profiles/config2_view_kernels.md).
 NCU_DRAM_BYTES = {
-    "preprocess": 284.1e6, "duplicate": 12.2e6, "blend_forward": 67.5e6,
-    "blend_backward": 132.8e6, "gaussian_backward": 497.9e6,
+    "preprocess": 285.4e6, "duplicate": 12.0e6, "blend_forward": 66.8e6,
+    "blend_backward": 133.5e6, "gaussian_backward": 460.5e6,
 }
 # warp instructions (smsp__inst_executed.sum) per launch of the blend kernels from the same
-# capture: the blends are bound by instruction issue (one warp instruction per cycle on each
+# captures: the blends are bound by instruction issue (one warp instruction per cycle on each
 # of the 4 x 148 schedulers), not by FP32 FMA throughput
-NCU_WARP_INST = {"blend_forward": 289.6e6, "blend_backward": 551.6e6}
+NCU_WARP_INST = {"blend_forward": 289.7e6, "blend_backward": 550.5e6}
 
 
 def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int,
