@@ -19,6 +19,7 @@
 // GPU global time, 5 s by default, and an iteration cap); a timeout sets kErrPeerTimeout and
 // the kernel returns.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "capi_internal.h"
@@ -163,8 +164,11 @@ __device__ __forceinline__ void mark_phase(const gs_shard_buffers& b, int k) {
   }
 }
 
+// Two CTAs per SM: the grid is two CTAs per SM and every CTA waits at the barriers for the CTA
+// of the same index on the other GPUs, so the whole grid must be resident at once; the launch
+// bound keeps the registers within what two CTAs of 256 threads may use.
 template <bool kMulticast>
-__global__ void __launch_bounds__(kShardThreads) sharded_adam_kernel(ShardArgs a) {
+__global__ void __launch_bounds__(kShardThreads, 2) sharded_adam_kernel(ShardArgs a) {
   const gs_shard_buffers& b = a.b;
   mark_phase(b, 0);
   if (!peer_barrier(a)) return;
@@ -250,13 +254,18 @@ __global__ void __launch_bounds__(kShardThreads) sharded_adam_kernel(ShardArgs a
   fence_proxy_alias();
 }
 
+// SM count of the current device, looked up once per device ordinal.
 int sm_count_cached() {
-  static int count = 0;
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> counts[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
+  int count = counts[dev].load(std::memory_order_relaxed);
   if (count == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
     if (count <= 0) count = 148;
+    counts[dev].store(count, std::memory_order_relaxed);
   }
   return count;
 }
