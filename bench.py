@@ -204,7 +204,7 @@ def barrier(world: int) -> None:
 # ---- per-stage timing ----------------------------------------------------------------------
 STAGES = {  # name: (start mark, end mark) of gs_set_stage_events
     "preprocess": (0, 1), "depth_sort": (1, 2), "duplicate": (2, 3), "tile_sort": (3, 4),
-    "tile_ranges": (4, 5), "blend_forward": (5, 6), "blend_backward": (7, 8),
+    "tile_order": (4, 5), "blend_forward": (5, 6), "blend_backward": (7, 8),
     "gaussian_backward": (8, 9),
 }
 N_MARKS = 10
@@ -526,7 +526,6 @@ def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n:
         "depth_sort": 4 * 16 * n,                   # 4 passes over (key, id) of N_v <= N
         "duplicate": 12 * n + 8 * mean_pairs,
         "tile_sort": 2 * 16 * mean_pairs,
-        "tile_ranges": 8 * mean_pairs,
         "gaussian_backward": 48 * n + 236 * n + 236 * n + 8 * n,
     }
     if name in hbm_bytes:

@@ -296,35 +296,6 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
   }
 }
 
-// Tile ranges from the tile-sorted keys (csrc/forward/rasterize.cu:146-165); ranges of
-// tiles with no pairs stay (0, 0) from the preceding memset.
-static __global__ void __launch_bounds__(256) tile_ranges_kernel(const unsigned* __restrict__ keys,
-                                                          const int* pair_count,
-                                                          long long pair_capacity,
-                                                          unsigned num_tiles,
-                                                          int2* __restrict__ ranges) {
-  const int M = *pair_count;
-  if ((long long)M > pair_capacity) return;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < M;
-       idx += gridDim.x * blockDim.x) {
-    const unsigned cur = keys[idx];
-    if (cur >= num_tiles || (idx > 0 && keys[idx - 1] >= num_tiles)) {
-      raise_device_error(kErrBadIndex);
-      continue;
-    }
-    if (idx == 0) {
-      ranges[cur].x = 0;
-    } else {
-      const unsigned prev = keys[idx - 1];
-      if (cur != prev) {
-        ranges[prev].y = idx;
-        ranges[cur].x = idx;
-      }
-    }
-    if (idx == M - 1) ranges[cur].y = M;
-  }
-}
-
 // Launch order of the blend CTAs: tiles by decreasing list length, so the long serial
 // walks of crowded tiles start first and the short ones fill in behind them (with raster
 // order a crowded tile that starts late sets the kernel's end). Lengths are bucketed by
@@ -340,16 +311,26 @@ __device__ __forceinline__ int tile_order_bucket(int K) {
   return 1 + 4 * lead + next2;
 }
 
+// It also finishes the tile ranges (csrc/forward/rasterize.cu:146-165: [start, end) of each
+// tile in the sorted pairs, empty tiles (0, 0)): with one tile the range is (0, M); otherwise the
+// final tile-sort pass left (start, -end) for every tile with pairs and kRangeUnset for the
+// others.
 static __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
-    const int2* __restrict__ ranges, const int* pair_count, long long pair_capacity,
-    int num_tiles, int* __restrict__ order) {
+    int2* __restrict__ ranges, const int* pair_count, long long pair_capacity, int num_tiles,
+    int* __restrict__ order) {
   __shared__ unsigned s_hist[kOrderBuckets];
   if ((long long)(*pair_count) > pair_capacity) return;  // the blend kernels return too
   const int tid = threadIdx.x;
   for (int b = tid; b < kOrderBuckets; b += kOrderThreads) s_hist[b] = 0u;
   __syncthreads();
+  const int M = *pair_count;
   for (int t = tid; t < num_tiles; t += kOrderThreads) {
-    const int2 r = ranges[t];
+    int2 r = ranges[t];
+    if (num_tiles == 1)
+      r = make_int2(0, M);
+    else
+      r = r.x == kRangeUnset ? make_int2(0, 0) : make_int2(r.x, -r.y);
+    ranges[t] = r;
     atomicAdd(&s_hist[tile_order_bucket(r.y - r.x)], 1u);
   }
   __syncthreads();

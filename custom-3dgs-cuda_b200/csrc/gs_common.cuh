@@ -135,6 +135,10 @@ __device__ __forceinline__ void blend_step(float alpha, float4 col, float& T, fl
 // ---------------------------------------------------------------------------------------
 // Decoupled look-back status words: bits [31:30] = flag, bits [29:0] = value.
 // ---------------------------------------------------------------------------------------
+// Initial value of both words of a tile range before the final tile-sort pass fills it in:
+// the byte pattern 0x7f, above any pair index.
+constexpr int kRangeUnset = 0x7f7f7f7f;
+
 constexpr unsigned kFlagAggregate = 1u << 30;
 constexpr unsigned kFlagPrefix = 2u << 30;
 constexpr unsigned kFlagMask = 3u << 30;

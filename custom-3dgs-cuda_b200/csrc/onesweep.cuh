@@ -32,6 +32,11 @@ struct SortPass {
   unsigned* ticket;            // tile ticket counter, zeroed before the sort
   int shift;                   // bit offset of this pass's digit
   unsigned mask;               // digit mask: (1 << digit bits) - 1, at most 255
+  // Final pass of the tile sort only (else null): the keys are tile ids, this pass's digit is
+  // their top digit, and each tile's [start, end) in the sorted order is written here as
+  // (start, -end), both initialised to kRangeUnset (see tile_order_kernel, which decodes them).
+  int2* ranges = nullptr;
+  unsigned num_tiles = 0;
 };
 
 static __global__ void __launch_bounds__(kSortThreads, 3) onesweep_pass_kernel(SortPass a) {
@@ -127,13 +132,38 @@ static __global__ void __launch_bounds__(kSortThreads, 3) onesweep_pass_kernel(S
   const int count = min(kSortTileItems, n - tile * kSortTileItems);
   for (int i = tid; i < count; i += kSortThreads) {
     const unsigned k = s_keys[i];
-    const unsigned gpos = s_global_off[(k >> a.shift) & a.mask] + i;
+    const unsigned dg = (k >> a.shift) & a.mask;
+    const unsigned gpos = s_global_off[dg] + i;
     if (gpos >= (unsigned)n) {  // only reachable after a look-back timeout
       raise_device_error(kErrBadIndex);
       continue;
     }
     if (a.keys_out) a.keys_out[gpos] = k;
     a.vals_out[gpos] = s_vals[i];
+    if (a.ranges) {
+      // Tile ranges. Within this tile of items each digit run lands contiguously in the
+      // output, and within a run the keys are sorted (the earlier passes left the lower digits
+      // in order and this one is stable), so a key change inside a run is exactly a tile's
+      // start and its predecessor's end. At a run's ends the neighbour in the output belongs
+      // to another tile of items: those candidates go through atomics (min of the starts, max
+      // of the ends), which any exact store also written for that tile agrees with.
+      if (k >= a.num_tiles) {
+        raise_device_error(kErrBadIndex);
+        continue;
+      }
+      const bool run_start = i == 0 || ((s_keys[i - 1] >> a.shift) & a.mask) != dg;
+      const bool run_end = i == count - 1 || ((s_keys[i + 1] >> a.shift) & a.mask) != dg;
+      if (run_start) {
+        atomicMin(&a.ranges[k].x, (int)gpos);
+      } else {
+        const unsigned prev = s_keys[i - 1];
+        if (prev != k) {
+          a.ranges[k].x = (int)gpos;
+          a.ranges[prev].y = -(int)gpos;
+        }
+      }
+      if (run_end) atomicMin(&a.ranges[k].y, -(int)(gpos + 1));
+    }
   }
 }
 

@@ -199,22 +199,19 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
       sp.ticket = &hdr->ticket_tile[pass];
       sp.shift = L.tile_shift[pass];
       sp.mask = L.tile_mask[pass];
+      const bool last = pass == P - 1;
+      sp.ranges = last ? reinterpret_cast<int2*>(tile_ranges) : nullptr;
+      sp.num_tiles = (unsigned)L.T;
+      if (last) sp.keys_out = nullptr;  // the ranges are written in this pass
       if (L.nt > 0) {
         onesweep_pass_kernel<<<(unsigned)L.nt, kSortThreads, 0, stream>>>(sp);
         GS_CHECK_LAUNCH();
       }
     }
     mark_stage(4, stream);
-    if (capacity > 0) {
-      const long long blocks = std::min<long long>((capacity + 255) / 256, (long long)sm_count() * 8);
-      tile_ranges_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
-          tk[P % 2], &hdr->pair_count, capacity, (unsigned)L.T,
-          reinterpret_cast<int2*>(tile_ranges));
-      GS_CHECK_LAUNCH();
-    }
   }
   int* tile_order = reinterpret_cast<int*>(ws + L.tile_order);
-  tile_order_kernel<<<1, kOrderThreads, 0, stream>>>(reinterpret_cast<const int2*>(tile_ranges),
+  tile_order_kernel<<<1, kOrderThreads, 0, stream>>>(reinterpret_cast<int2*>(tile_ranges),
                                                       &hdr->pair_count, capacity, (int)L.T,
                                                       tile_order);
   GS_CHECK_LAUNCH();
@@ -253,7 +250,7 @@ int launch_rasterize(const RasterLayout& L, int N, int H, int W, const float* de
                      cudaStream_t stream) {
   RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
   GS_CUDA(cudaMemsetAsync(ws, 0, L.zero_bytes, stream));
-  GS_CUDA(cudaMemsetAsync(tile_ranges, 0, (size_t)L.T * 2 * sizeof(int), stream));
+  GS_CUDA(cudaMemsetAsync(tile_ranges, 0x7f, (size_t)L.T * 2 * sizeof(int), stream));  // kRangeUnset
   if (N > 0) {
     BinParams bp;
     fill_bin_params(bp, L, ws, N, H, W, depths, mean2d, cov2d, colors, alpha, capacity);

@@ -259,7 +259,7 @@ extern "C" int gs_render_forward(int N, int H, int W, const float* mu, const flo
   cudaStream_t st = (cudaStream_t)stream;
   RasterHeader* hdr = reinterpret_cast<RasterHeader*>(ws + L.header);
   GS_CUDA(cudaMemsetAsync(ws, 0, L.zero_bytes, st));
-  GS_CUDA(cudaMemsetAsync(tile_ranges, 0, (size_t)L.T * 2 * sizeof(int), st));
+  GS_CUDA(cudaMemsetAsync(tile_ranges, 0x7f, (size_t)L.T * 2 * sizeof(int), st));  // kRangeUnset
   mark_stage(0, st);
   if (N > 0) {
     PreprocessParams pp;
