@@ -616,6 +616,14 @@ def cpu_adam_seconds(scene) -> float:
     return time.perf_counter() - t0
 
 
+def bench_config(args, world: int) -> dict:
+    """The workload both arms report (the reference arm times a bounded sample of it on the
+    host cores; its `cpu_baseline.sample` says which)."""
+    return {"workload": WORKLOAD, "gaussians": args.gaussians, "batch_views": BATCH_VIEWS,
+            "resolution": "1920x1080", "parallelism": f"views sharded over {world} rank(s)",
+            "l2": "inputs larger than L2 (236 MB of parameters + 25 MB per target)"}
+
+
 # ---- main -------------------------------------------------------------------------------------
 def run_reference(args, rank, world):
     """Reference arm: the reference has no CPU implementation of the path, so its CPU
@@ -624,7 +632,7 @@ def run_reference(args, rank, world):
         return
     from gs3d_b200 import scenes
 
-    sc, targets = scenes.config4(0, n=N_GAUSSIANS, n_views=BATCH_VIEWS)
+    sc, targets = scenes.config4(0, n=args.gaussians, n_views=BATCH_VIEWS)
     adam_s = cpu_adam_seconds(sc)
     for _ in range(args.warmup_ref):
         cpu_baseline_sample(sc, sc.views[0], targets[0], adam_s)
@@ -640,7 +648,7 @@ def run_reference(args, rank, world):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample": "one view per step", "inputs": "host"},
+            "config": bench_config(args, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": res["cores"], "kind": "port",
                              "sample": res["sample"]},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -870,9 +878,7 @@ def run_ours(args, rank, world, local) -> int:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "gaussians": args.gaussians, "batch_views": BATCH_VIEWS,
-                   "resolution": "1920x1080", "parallelism": f"views sharded over {world} rank(s)",
-                   "l2": "inputs larger than L2 (236 MB of parameters + 25 MB per target)"},
+        "config": bench_config(args, world),
         "per_view_config2": breakdown,
         "stage_ms_per_view": stage_ms,
         "view_streams": len(trainer._streams) or 1,
