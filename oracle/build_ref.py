@@ -63,7 +63,7 @@ def build(reference: Path = DEFAULT_REFERENCE, verbose: bool = False) -> list[Pa
     full = [csrc / f for f in FULL_SOURCES]
     if not all(p.exists() for p in full):
         return []
-    os.environ.setdefault("MAX_JOBS", "4")
+    os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 4))
     inc = [csrc, csrc / "forward", csrc / "backward"]
     built = [
         _load("ref_raster", [HERE / "ref_raster_bind.cpp", *raster], inc, verbose),
