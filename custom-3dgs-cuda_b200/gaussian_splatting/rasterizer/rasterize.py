@@ -26,7 +26,11 @@ class RasterizeFunction(t.autograd.Function):
     """Projection -> SH colour -> tile binning/sort -> alpha blend, and the reverse.
 
     Runs the fused render path (custom_rasterizer_cuda.render: two C-ABI calls per direction
-    instead of the reference's six ops); its outputs equal chaining the six ops.
+    instead of the reference's six ops); its outputs equal chaining the six ops. It bins each
+    splat only into the tiles where it can pass the opacity test (GS_RENDER_TIGHT_BINS): the
+    pairs it drops fail that test at every pixel of their tile, so the image, transmittance,
+    radii and gradients are those of the reference's binning, from shorter tile lists (the
+    lists themselves are not outputs of this function).
     """
 
     last_mean2d_grad: t.Tensor | None = None
@@ -61,7 +65,7 @@ class RasterizeFunction(t.autograd.Function):
         cam_position = (-t.matmul(cam_rotation.T, cam_translation)).reshape(3).contiguous()
         img, radii, state = render_forward(mu, q, s, alpha, albedo, k_j, cam_rotation,
                                            cam_translation, cam_position, fx_f, fy_f, cx_f, cy_f,
-                                           img_h, img_w)
+                                           img_h, img_w, tight_bins=True)
         RasterizeFunction.last_radii2d = radii
         ctx.save_for_backward(mu, q, s, alpha, albedo, k_j, cam_rotation, cam_translation,
                               cam_position)
