@@ -9,7 +9,8 @@ import numpy as np
 import pytest
 import torch
 
-from test_gpu_parity import assert_grad_close, np32, scenes_small
+from test_gpu_parity import (assert_grad_close, assert_like_reference_nondeterminism, np32,
+                             scenes_small)
 
 pytestmark = pytest.mark.gpu
 
@@ -91,7 +92,20 @@ def test_rasterize_function_attributes(cuda_device):
     assert g.alpha.grad.shape == g.alpha.shape and torch.isfinite(g.alpha.grad).all()
 
 
-@pytest.mark.parametrize("case", list(scenes_small()), ids=lambda c: c[0])
+def elongated_scene():
+    """Needle-like splats (one axis about 12x the others, random orientations) of a few to a
+    few dozen tiles: tilted opacity ellipses whose extent boxes are much larger than they are."""
+    from gs3d_b200 import scenes
+
+    g = torch.Generator("cpu").manual_seed(21)
+    n = 20_000
+    means = torch.rand(n, 3, generator=g) * 4.0 - 2.0
+    sc = scenes.Scene("needles20k", *scenes._draw(g, n, means, -4.0, 0.3))
+    sc.s[:, 0] += 2.5
+    return "needles20k_640x360", sc, scenes.pinhole((0.5, 0.3, 7.0), 640, 360, 500.0)
+
+
+@pytest.mark.parametrize("case", list(scenes_small()) + [elongated_scene()], ids=lambda c: c[0])
 def test_tight_bins_keep_image_and_gradients(crc, cuda_device, case):
     """GS_RENDER_TIGHT_BINS: image, transmittance and radii identical to the reference binning,
     gradients within the atomic-order tolerance, and never more pairs."""
@@ -117,8 +131,25 @@ def test_tight_bins_keep_image_and_gradients(crc, cuda_device, case):
     assert torch.equal(img0, img1) and torch.equal(st0.final_T, st1.final_T)
     assert torch.equal(radii0, radii1)
     assert st1.pairs <= st0.pairs
-    for a, b, what in zip(g1, g0, ("mu", "q", "s", "opacity", "A", "kj", "mean2d")):
-        assert_grad_close(np32(a), np32(b), what + " (tight bins)")
+    names = ("mu", "q", "s", "opacity", "A", "kj", "mean2d")
+    if not case[0].startswith("needles"):
+        for a, b, what in zip(g1, g0, names):
+            assert_grad_close(np32(a), np32(b), what + " (tight bins)")
+        return
+    # Near-singular 2D covariances amplify the order of the float atomics in the mean, rotation
+    # and log-scale gradients beyond a flat 1e-4 (two runs of the same binning differ there
+    # too): those must differ from the reference binning's first run by no more than its own
+    # other runs do (assert_like_reference_nondeterminism), the rest within 1e-4.
+    st0 = render_forward(mu, q, s, op, A, kj, R, t, cam, view.fx, view.fy, view.cx, view.cy,
+                         view.height, view.width)[2]
+    runs = [g0] + [render_backward(st0, grad_img, mu, q, s, A, kj, R, t, cam, view.fx, view.fy,
+                                   view.cx, view.cy) for _ in range(3)]
+    for k, what in enumerate(names):
+        if what in ("mu", "q", "s"):
+            assert_like_reference_nondeterminism(np32(g1[k]), [np32(r[k]) for r in runs],
+                                                 what + " (tight bins)")
+        else:
+            assert_grad_close(np32(g1[k]), np32(g0[k]), what + " (tight bins)")
 
 
 def test_pair_buffers_sized_from_the_last_count(cuda_device):
