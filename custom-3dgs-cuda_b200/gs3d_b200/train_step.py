@@ -188,7 +188,8 @@ class Trainer:
     statistics are updated inside the per-Gaussian backward kernel and the opacity gradient is
     taken through the sigmoid once per step. Consecutive views run on `view_streams`
     alternating CUDA streams (1 = all on the current stream), the blend kernels then in their
-    throughput variants (GS_RENDER_CONCURRENT), and with `tight_bins` the splats are binned
+    throughput variants (GS_RENDER_CONCURRENT) when the rank has more than one view of the
+    batch, and with `tight_bins` the splats are binned
     only into tiles where they can pass the opacity test (same images and gradients, shorter
     tile lists). mode "autograd" runs the same step through
     `gaussian_splatting.rasterizer.rasterize` (the drop-in RasterizeFunction) and
@@ -261,8 +262,12 @@ class Trainer:
                 self._streams = [torch.cuda.Stream(device) for _ in range(view_streams)]
                 self._accum_events = [_lib.Event(), _lib.Event()]
         # views overlap on streams: the blend kernels' throughput variants (also in steps
-        # whose views run in order, so that per-stage timings see the same kernels)
-        self.concurrent_views = len(self._streams) > 1
+        # whose views run in order, so that per-stage timings see the same kernels). A rank
+        # with one view of the batch overlaps nothing and takes the single-view variants: alone
+        # their time varies less with the view (on B200, across config-4 views, backward
+        # 0.79-0.80 ms against 0.73-0.96 ms for the four-pixel variant), and the step waits for
+        # the slowest rank.
+        self.concurrent_views = len(self._streams) > 1 and len(self.plan.views()) > 1
 
     def _update(self) -> None:
         """Batch-mean gradients across ranks, then Adam. The sharded step does both (and the
