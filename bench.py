@@ -205,9 +205,9 @@ def barrier(world: int) -> None:
 STAGES = {  # name: (start mark, end mark) of gs_set_stage_events
     "preprocess": (0, 1), "depth_sort": (1, 2), "duplicate": (2, 3), "tile_sort": (3, 4),
     "tile_order": (4, 5), "blend_forward": (5, 6), "blend_backward": (7, 8),
-    "gaussian_backward": (8, 9),
+    "gaussian_backward": (10, 9),
 }
-N_MARKS = 10
+N_MARKS = 11
 
 
 class StageTimer:
@@ -228,10 +228,18 @@ class StageTimer:
     def remove(self) -> None:
         self._lib.set_stage_events(None)
 
-    def stage_ms(self) -> dict:
+    def stage_ms(self, combined_views: int = 0) -> dict:
+        """Mean ms per view of each stage. With `combined_views` = V > 0 the per-Gaussian
+        backward ran once per step over the step's V views, while the last view's events were
+        installed: its time is taken from every V-th set and divided by V."""
         out = {}
+        sets = self.sets[:self.used]
         for name, (a, b) in STAGES.items():
-            vals = [ev[a].elapsed_ms(ev[b]) for ev in self.sets[:self.used]]
+            if name == "gaussian_backward" and combined_views:
+                vals = [ev[a].elapsed_ms(ev[b]) / combined_views
+                        for ev in sets[combined_views - 1::combined_views]]
+            else:
+                vals = [ev[a].elapsed_ms(ev[b]) for ev in sets]
             out[name] = statistics.mean(vals) if vals else None
         return out
 
@@ -511,6 +519,7 @@ NCU_WARP_INST = {"blend_forward": 289.7e6, "blend_backward": 550.5e6}
 
 
 def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n: int,
+                   combined_views: int = 0,
                    name: str | None = None) -> dict:
     """Roofline of one stage (default: the dominant one) over the timed region. The blends are
     FP32-issue bound (no dense contraction anywhere on the path); the per-Gaussian stages are
@@ -526,7 +535,10 @@ def roofline_entry(stage_ms: dict, stats: dict, n_views_timed: int, pk: dict, n:
         "depth_sort": 4 * 16 * n,                   # 4 passes over (key, id) of N_v <= N
         "duplicate": 12 * n + 8 * mean_pairs,
         "tile_sort": 2 * 16 * mean_pairs,
-        "gaussian_backward": 48 * n + 236 * n + 236 * n + 8 * n,
+        # per view: its blend sums in; parameters in, gradients out (read-modify-write after
+        # the first view) and statistics, once per view, or once per step over V views
+        "gaussian_backward": (48 * n + (232 * n + 236 * n + 24 * n) / combined_views
+                              if combined_views else 48 * n + 236 * n + 236 * n + 8 * n),
     }
     if name in hbm_bytes:
         achieved = hbm_bytes[name] / (ms * 1e-3) / 1e9
@@ -829,7 +841,7 @@ def run_ours(args, rank, world, local) -> int:
         trainer.step(before_view=lambda vi: timer.install_next())
     torch.cuda.synchronize()
     timer.remove()
-    stage_ms = timer.stage_ms()
+    stage_ms = timer.stage_ms(len(mine) if trainer.combined_backward else 0)
     total_launches = int(sum_over_ranks(float(launches), world))
 
     # ---- e2e: every step copies its targets from pinned host memory (side stream, each view's
@@ -886,6 +898,8 @@ def run_ours(args, rank, world, local) -> int:
         "blend_variant": ("throughput: 2 / 4 pixels per thread forward / backward"
                           if trainer.concurrent_views else
                           "latency: 1 / 2 pixels per thread forward / backward"),
+        "per_gaussian_backward": ("once per step over the rank's views"
+                                  if trainer.combined_backward else "once per view"),
         "update_ms_per_step": update_ms,
         "update_phases_ms_rank0": update_phases,
         "update": ("fused reduce-scatter + sharded Adam + all-gather (multicast)"
@@ -898,7 +912,8 @@ def run_ours(args, rank, world, local) -> int:
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d_bytes * world,
                 "d2h_bytes_per_step": 4 * world},
-        "roofline": roofline_entry(stage_ms, stats, args.steps * len(mine), pk, args.gaussians),
+        "roofline": roofline_entry(stage_ms, stats, args.steps * len(mine), pk, args.gaussians,
+                                   len(mine) if trainer.combined_backward else 0),
         "roofline_blend_forward": roofline_entry(stage_ms, stats, args.steps * len(mine), pk,
                                                  args.gaussians, name="blend_forward"),
     }

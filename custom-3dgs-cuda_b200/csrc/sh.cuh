@@ -155,4 +155,36 @@ __device__ __forceinline__ float3 sh_backward_inplace(float3 gcol, float3 mu, fl
                      inv_len * (gd.z - dz * ddot));
 }
 
+// sh_backward_inplace for one of several views: the coefficients kj are left unchanged and
+// this view's dL/dk_j (the values sh_backward_inplace writes, each rounded as a product) is
+// added to gkj, so that views summed in order give what one in-place call per view, summed
+// into a buffer in the same order, gives.
+__device__ __forceinline__ float3 sh_backward_accumulate(float3 gcol, float3 mu, float3 cam,
+                                                         float3 A, const float* kj,
+                                                         float* gkj, float3& gA) {
+  const float vx = mu.x - cam.x, vy = mu.y - cam.y, vz = mu.z - cam.z;
+  const float inv_len = rsqrtf(vx * vx + vy * vy + vz * vz + 1e-8f);
+  const float dx = vx * inv_len, dy = vy * inv_len, dz = vz * inv_len;
+  float Y[kShRest];
+  sh_basis(dx, dy, dz, Y);
+  const float3 rgb = sh_unclamped(Y, A, kj);
+  const float g0 = (rgb.x < 0.0f || rgb.x > 1.0f) ? 0.0f : gcol.x;
+  const float g1 = (rgb.y < 0.0f || rgb.y > 1.0f) ? 0.0f : gcol.y;
+  const float g2 = (rgb.z < 0.0f || rgb.z > 1.0f) ? 0.0f : gcol.z;
+  gA = make_float3(g0 * kShC0, g1 * kShC0, g2 * kShC0);
+  float dY[kShRest];
+#pragma unroll
+  for (int k = 0; k < kShRest; ++k) {
+    const float k0 = kj[k * 3 + 0], k1 = kj[k * 3 + 1], k2 = kj[k * 3 + 2];
+    gkj[k * 3 + 0] = __fadd_rn(gkj[k * 3 + 0], __fmul_rn(g0, Y[k]));
+    gkj[k * 3 + 1] = __fadd_rn(gkj[k * 3 + 1], __fmul_rn(g1, Y[k]));
+    gkj[k * 3 + 2] = __fadd_rn(gkj[k * 3 + 2], __fmul_rn(g2, Y[k]));
+    dY[k] = g0 * k0 + g1 * k1 + g2 * k2;
+  }
+  const float3 gd = sh_basis_backward(dx, dy, dz, dY);
+  const float ddot = dx * gd.x + dy * gd.y + dz * gd.z;
+  return make_float3(inv_len * (gd.x - dx * ddot), inv_len * (gd.y - dy * ddot),
+                     inv_len * (gd.z - dz * ddot));
+}
+
 }  // namespace gs

@@ -50,6 +50,10 @@ SIGNATURES = {
                                    c_float, c_float, c_float, P, c_longlong, P, P, P, P, P,
                                    c_size_t, P, P, P, P, P, P, P, c_int, P, P, P, c_float,
                                    c_float, P, P, c_uint, P]),
+    "gs_render_backward_blend": (c_int, [c_int, c_int, c_int, P, P, c_longlong, P, P, P, P, P,
+                                         c_size_t, c_uint, P]),
+    "gs_render_backward_gaussians": (c_int, [c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P,
+                                             c_int, P, P, P, P]),
     "gs_l1_ssim_workspace_size": (c_size_t, [c_int, c_int]),
     "gs_l1_ssim_forward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
     "gs_l1_ssim_backward": (c_int, [c_int, c_int, P, P, c_float, P, c_size_t, P, P, P]),
@@ -72,6 +76,18 @@ SIGNATURES = {
     "gs_device_error_bits": (c_int, [POINTER(c_uint)]),
     "gs_clear_device_errors": (c_int, []),
 }
+
+
+GS_MAX_VIEWS_PER_CALL = 16
+
+
+class ViewSums(ctypes.Structure):
+    """Mirror of gs_view_sums (include/gs3d_b200.h): one view's blend-backward workspace and
+    camera for gs_render_backward_gaussians."""
+
+    _fields_ = [("workspace", c_void_p), ("R", c_void_p), ("t", c_void_p), ("cam_pos", c_void_p),
+                ("fx", c_float), ("fy", c_float), ("cx", c_float), ("cy", c_float),
+                ("stat_scale_x", c_float), ("stat_scale_y", c_float)]
 
 
 def load(path: Path = LIB_PATH) -> ctypes.CDLL:

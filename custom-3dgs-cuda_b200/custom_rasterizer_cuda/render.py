@@ -9,6 +9,7 @@ does (gaussian_splatting/rasterizer/rasterize.py:43-117).
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -201,3 +202,52 @@ def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, c
             accum_done.handle if accum_done is not None else None,
             state.backward_flags, _stream(dev)))
     return (*out, g_mean2d)
+
+
+def backward_workspace(n: int, device) -> torch.Tensor:
+    """A workspace for one view's render_backward_blend sums (3 float4 per Gaussian)."""
+    return torch.empty((lib.gs_render_backward_workspace_size(int(n)),), device=device,
+                       dtype=torch.uint8)
+
+
+def render_backward_blend(state: RenderState, grad_img, n: int, workspace=None) -> torch.Tensor:
+    """First half of render_backward for one of several views: the blend backward of the view
+    rendered into `state`, leaving its per-Gaussian sums in `workspace` (backward_workspace(n),
+    allocated when None), which is returned for render_backward_views."""
+    dev = state.final_T.device
+    if workspace is None:
+        workspace = backward_workspace(n, dev)
+    grad_img = grad_img.contiguous()
+    with torch.cuda.device(dev):
+        check(lib.gs_render_backward_blend(
+            int(n), state.height, state.width, _ptr(grad_img), state.workspace.data_ptr(),
+            state.capacity, state.sorted_ids.data_ptr(), _ptr(state.tile_ranges),
+            _ptr(state.final_T), _ptr(state.n_contrib), workspace.data_ptr(),
+            workspace.numel(), state.backward_flags, _stream(dev)))
+    return workspace
+
+
+def render_backward_views(views, mu, q, s, albedo, k_j, out, accumulate: bool = False,
+                          stats=None) -> None:
+    """Second half of render_backward for several views at once: `views` is a list of
+    (workspace from render_backward_blend, R, t, cam_pos, fx, fy, cx, cy, stat_scale_x,
+    stat_scale_y); the six gradient buffers `out` get the views' gradients summed in list order,
+    after their own values (`accumulate`) or zero, with the same bits as one render_backward per
+    view accumulating in that order. `stats` = (norm_sum, count, norm_max) as in render_backward,
+    each view with its own scales. Up to GS_MAX_VIEWS_PER_CALL views per launch."""
+    from ._lib import GS_MAX_VIEWS_PER_CALL, ViewSums
+
+    N = int(mu.shape[0])
+    dev = mu.device
+    st = (None, None, None) if stats is None else tuple(_ptr(x) for x in stats[:3])
+    with torch.cuda.device(dev):
+        for c0 in range(0, len(views), GS_MAX_VIEWS_PER_CALL):
+            chunk = views[c0:c0 + GS_MAX_VIEWS_PER_CALL]
+            arr = (ViewSums * len(chunk))()
+            for k, (ws, R, t, cam, fx, fy, cx, cy, sx, sy) in enumerate(chunk):
+                arr[k] = ViewSums(ws.data_ptr(), _ptr(R), _ptr(t), _ptr(cam), float(fx),
+                                  float(fy), float(cx), float(cy), float(sx), float(sy))
+            check(lib.gs_render_backward_gaussians(
+                N, len(chunk), ctypes.addressof(arr), _ptr(mu), _ptr(q), _ptr(s), _ptr(albedo),
+                _ptr(k_j), *(_ptr(o) for o in out), 1 if (accumulate or c0 > 0) else 0, *st,
+                _stream(dev)))

@@ -203,6 +203,41 @@ GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const 
                               void* stream);
 
 /*
+ * gs_render_backward in two halves, for a batch of views whose gradients are summed (the
+ * training step). gs_render_backward_blend runs one view's blend backward and leaves its
+ * per-Gaussian sums in `workspace` (gs_render_backward_workspace_size(N) bytes, one per view,
+ * kept until the second half has read it). gs_render_backward_gaussians then runs the SH and
+ * projection backward of up to GS_MAX_VIEWS_PER_CALL views in one pass over the Gaussians:
+ * each parameter, gradient and statistic element is read and written once per call instead of
+ * once per view. The views are summed in array order after the buffers' own values
+ * (accumulate = 1) or after zero (accumulate = 0), with the same rounding as one
+ * gs_render_backward per view accumulating into the buffers in that order; so calls over
+ * consecutive groups of views (the later ones with accumulate = 1) give the same bits as one
+ * call over all of them. Statistics as gs_render_backward, per view with its own scales.
+ */
+#define GS_MAX_VIEWS_PER_CALL 16
+typedef struct gs_view_sums {
+  const void* workspace;  /* the view's gs_render_backward_blend workspace */
+  const float* R;         /* [3, 3] device, the view's camera as in gs_render_forward */
+  const float* t;         /* [3] device */
+  const float* cam_pos;   /* [3] device */
+  float fx, fy, cx, cy;
+  float stat_scale_x, stat_scale_y;
+} gs_view_sums;
+GS_API int gs_render_backward_blend(int N, int H, int W, const float* grad_img,
+                                    const void* fwd_workspace, long long pair_capacity,
+                                    const int* sorted_ids, const int* tile_ranges,
+                                    const float* final_T, const int* n_contrib, void* workspace,
+                                    size_t workspace_bytes, unsigned flags, void* stream);
+GS_API int gs_render_backward_gaussians(int N, int n_views, const gs_view_sums* views,
+                                        const float* mu, const float* q, const float* s,
+                                        const float* albedo, const float* k_j, float* g_mu,
+                                        float* g_q, float* g_s, float* g_opacity,
+                                        float* g_albedo, float* g_k_j, int accumulate,
+                                        float* stat_norm_sum, float* stat_count,
+                                        float* stat_max, void* stream);
+
+/*
  * Fused photometric loss of the training step (no counterpart in the reference's extension;
  * the reference trainer computes it with torchmetrics, gaussian_splatting/utils/loss.py:12-33):
  * loss = (1 - lambda) * mean|img - target| + lambda * (1 - SSIM) over [H, W, 3] images, with
@@ -345,9 +380,11 @@ GS_API int gs_event_destroy(void* event);
  * installed, gs_render_forward / gs_render_backward record events[k] on their stream at stage
  * boundaries: 0 forward start, 1 after preprocess, 2 after the depth sort, 3 after pair
  * duplication, 4 after the tile sort, 5 after tile ranges, 6 after the blend, 7 backward start
- * (after the accumulator clear), 8 after the blend backward, 9 after the per-Gaussian
- * backward. The setting is process-wide; events = NULL or n = 0 removes it. Timed events come
- * from gs_event_create_timed and are read with gs_event_elapsed_ms.
+ * (after the accumulator clear), 8 after the blend backward, 10 before and 9 after the
+ * per-Gaussian backward (gs_render_backward, or gs_render_backward_gaussians for several views;
+ * gs_render_backward_blend records 7 and 8). The setting is process-wide; events = NULL or
+ * n = 0 removes it. Timed events come from gs_event_create_timed and are read with
+ * gs_event_elapsed_ms.
  */
 GS_API int gs_set_stage_events(void* const* events, int n);
 GS_API int gs_event_create_timed(void** event);

@@ -177,3 +177,64 @@ def test_pair_buffers_sized_from_the_last_count(cuda_device):
     _, _, st0 = render(sc0, sc0.views[0])
     tiles = ((sc0.views[0].width + 15) // 16) * ((sc0.views[0].height + 15) // 16)
     assert st0.capacity == sc0.N * tiles and st0.pairs <= st0.capacity
+
+
+def test_combined_per_gaussian_backward_over_views(cuda_device):
+    """gs_render_backward_blend + gs_render_backward_gaussians (the training step's backward):
+    one call over four views gives the same bits as one call per view accumulating in view
+    order and as two calls over two views each; and it agrees (atomic-order tolerance) with one
+    render_backward per view accumulating into the same buffers, statistics included."""
+    from custom_rasterizer_cuda.render import (render_backward, render_backward_blend,
+                                               render_backward_views, render_forward)
+    from gs3d_b200 import scenes
+
+    dev = cuda_device
+    sc = scenes.config2(5, n=60_000)
+    eyes = ((0.0, 0.0, 8.0), (6.0, 1.0, 5.0), (-5.0, 3.0, -6.0), (1.0, -7.0, 4.0))
+    views = [scenes.pinhole(e, 480, 270, 375.0) for e in eyes]
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    op = torch.sigmoid(al).reshape(-1).contiguous()
+    N = sc.N
+    g = torch.Generator("cpu").manual_seed(7)
+    grads = [torch.rand(v.height, v.width, 3, generator=g).to(dev) for v in views]
+    cams, sums, states = [], [], []
+    for v, gi in zip(views, grads):
+        R, t = v.R.to(dev).contiguous(), v.T.to(dev).contiguous()
+        cam = (-torch.matmul(R.T, t)).reshape(3).contiguous()
+        _, _, st = render_forward(mu, q, s, op, A, kj, R, t, cam, v.fx, v.fy, v.cx, v.cy,
+                                  v.height, v.width, tight_bins=True)
+        sums.append(render_backward_blend(st, gi, N))
+        cams.append((R, t, cam))
+        states.append(st)
+    entries = [(ws, R, t, cam, v.fx, v.fy, v.cx, v.cy, v.width / 2.0, v.height / 2.0)
+               for ws, (R, t, cam), v in zip(sums, cams, views)]
+
+    def fresh():
+        f32 = dict(device=dev, dtype=torch.float32)
+        out = (torch.full((N, 3), 7.0, **f32), torch.full((N, 4), 7.0, **f32),
+               torch.full((N, 3), 7.0, **f32), torch.full((N,), 7.0, **f32),
+               torch.full((N, 3), 7.0, **f32), torch.full((N, 15, 3), 7.0, **f32))
+        stats = (torch.zeros(N, **f32), torch.zeros(N, **f32), torch.zeros(N, **f32))
+        return out, stats
+
+    out_all, st_all = fresh()
+    render_backward_views(entries, mu, q, s, A, kj, out_all, stats=st_all)
+    out_one, st_one = fresh()
+    for k, e in enumerate(entries):
+        render_backward_views([e], mu, q, s, A, kj, out_one, accumulate=k > 0, stats=st_one)
+    out_two, st_two = fresh()
+    render_backward_views(entries[:2], mu, q, s, A, kj, out_two, stats=st_two)
+    render_backward_views(entries[2:], mu, q, s, A, kj, out_two, accumulate=True, stats=st_two)
+    for a, b, c in zip(out_all + st_all, out_one + st_one, out_two + st_two):
+        assert torch.equal(a, b) and torch.equal(a, c)
+    assert int((st_all[1] > 0).sum()) > N // 2  # most Gaussians are seen by some view
+
+    # against render_backward per view (its own blend pass: the same sums up to atomic order)
+    out_ref, st_ref = fresh()
+    for k, (v, gi, st, (R, t, cam)) in enumerate(zip(views, grads, states, cams)):
+        render_backward(st, gi, mu, q, s, A, kj, R, t, cam, v.fx, v.fy, v.cx, v.cy,
+                        want_mean2d_grad=False, out=out_ref, accumulate=k > 0,
+                        stats=(*st_ref, v.width / 2.0, v.height / 2.0))
+    names = ("mu", "q", "s", "opacity", "A", "kj", "norm_sum", "count", "norm_max")
+    for a, b, what in zip(out_all + st_all, out_ref + st_ref, names):
+        assert_grad_close(np32(a), np32(b), what + " (combined over views)")
