@@ -9,8 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from test_gpu_parity import (assert_grad_close, assert_like_reference_nondeterminism, np32,
-                             scenes_small)
+from test_gpu_parity import assert_grad_close, np32, scenes_small
 
 pytestmark = pytest.mark.gpu
 
@@ -137,19 +136,20 @@ def test_tight_bins_keep_image_and_gradients(crc, cuda_device, case):
             assert_grad_close(np32(a), np32(b), what + " (tight bins)")
         return
     # Near-singular 2D covariances amplify the order of the float atomics in the mean, rotation
-    # and log-scale gradients beyond a flat 1e-4 (two runs of the same binning differ there
-    # too): those must differ from the reference binning's first run by no more than its own
-    # other runs do (assert_like_reference_nondeterminism), the rest within 1e-4.
-    st0 = render_forward(mu, q, s, op, A, kj, R, t, cam, view.fx, view.fy, view.cx, view.cy,
-                         view.height, view.width)[2]
-    runs = [g0] + [render_backward(st0, grad_img, mu, q, s, A, kj, R, t, cam, view.fx, view.fy,
-                                   view.cx, view.cy) for _ in range(3)]
-    for k, what in enumerate(names):
+    # and log-scale gradients beyond a flat 1e-4 per element (the two binnings' tile lists
+    # differ, so their blend CTAs and atomics run in different orders): those are bounded in
+    # aggregate (relative L2 1e-3, at most 1% of the elements beyond the 1e-4 band), the rest
+    # per element. tests/test_gpu_parity.py compares needle gradients, tight bins included,
+    # with the reference's own kernels.
+    for a, b, what in zip(g1, g0, names):
+        a64, b64 = np32(a).astype(np.float64), np32(b).astype(np.float64)
         if what in ("mu", "q", "s"):
-            assert_like_reference_nondeterminism(np32(g1[k]), [np32(r[k]) for r in runs],
-                                                 what + " (tight bins)")
+            rel_l2 = np.linalg.norm(a64 - b64) / np.linalg.norm(b64)
+            rms = np.sqrt(np.mean(b64 * b64))
+            beyond = int((np.abs(a64 - b64) > 1e-4 * (np.abs(b64) + rms)).sum())
+            assert rel_l2 <= 1e-3 and beyond <= 0.01 * b64.size, (what, rel_l2, beyond)
         else:
-            assert_grad_close(np32(g1[k]), np32(g0[k]), what + " (tight bins)")
+            assert_grad_close(a64, b64, what + " (tight bins)")
 
 
 def test_pair_buffers_sized_from_the_last_count(cuda_device):
