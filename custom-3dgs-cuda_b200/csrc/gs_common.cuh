@@ -14,6 +14,7 @@ constexpr unsigned kErrLookbackTimeout = 1u;  // a decoupled look-back wait hit 
 constexpr unsigned kErrCapacity = 2u;         // pair count exceeded the pair capacity
 constexpr unsigned kErrBadIndex = 4u;         // an index was out of range
 constexpr unsigned kErrPeerTimeout = 8u;      // a cross-GPU barrier wait hit its limit
+constexpr unsigned kErrCopyTimeout = 16u;     // a wait for a tensor-memory-accelerator copy hit its limit
 
 // Iteration limit of every spin-wait. Each iteration is one L2 round trip plus a short
 // sleep, so the limit bounds a wait to well under a second.

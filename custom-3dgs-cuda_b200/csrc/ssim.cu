@@ -24,8 +24,11 @@
 // Backward: the same tiling, a channel at a time, blurs A, B, Cm and combines them with x,
 // y and sign(x - y). One channel's planes (41 KB / 37 KB of shared memory) leave room for 5-6
 // CTAs per SM.
+#include <cstring>
+
 #include "capi_internal.h"
 #include "gs_common.cuh"
+#include "tma.cuh"
 
 namespace gs {
 
@@ -40,6 +43,13 @@ constexpr float kSsimC1 = 0.01f * 0.01f, kSsimC2 = 0.03f * 0.03f;
 static_assert(kSsimTW % kSsimRun == 0 && kSsimTH % kSsimRun == 0, "runs tile the output");
 static_assert(kSsimTW * (kSsimTH / kSsimRun) == kSsimThreads,
               "one vertical run per thread and channel");
+// The backward's halo box: columns bx - 8 .. bx + 39 (its start a multiple of 4 floats, as a
+// tile copy's innermost coordinate must be), the 5-pixel halo starting at offset 3.
+constexpr int kSsimBoxW = 48, kSsimBoxOff = 3;
+static_assert(kSsimBoxOff + kSsimInW <= kSsimBoxW && (kSsimBoxOff + kSsimR) % 4 == 0,
+              "the box covers the halo from a 16-byte aligned column");
+constexpr unsigned kSsimBoxBytes = 3u * kSsimInH * kSsimBoxW * sizeof(float);
+constexpr unsigned long long kCopyWaitNs = 1000000000ull;  // 1 s for a tile copy to land
 
 __constant__ float c_gauss[kSsimTaps];
 
@@ -51,10 +61,12 @@ struct SsimForwardSmem {
   double part[2][kSsimWarps];
 };
 
-// One channel at a time: its A, B, Cm planes and their horizontal blurs.
-struct SsimBackwardSmem {
-  float m[3][kSsimInH][kSsimInW];
+// One channel at a time: its A, B, Cm planes (halo box, 128-byte aligned: a tile copy's
+// destination) and their horizontal blurs.
+struct __align__(128) SsimBackwardSmem {
+  float m[3][kSsimInH][kSsimBoxW];
   float h[3][kSsimInH][kSsimTW];
+  uint64_t bar;  // completion of the tile copies (mbarrier)
 };
 
 // out[o] = sum_t g[t] in[o + t] for a run of kSsimRun outputs (registers only).
@@ -78,6 +90,23 @@ __device__ __forceinline__ void load_row_window(const float* row, float (&w)[kSs
   }
 }
 
+// The window of a run of the backward's halo box: `row` points at the run's first output
+// column (16-byte aligned), the window starts kSsimBoxOff further.
+__device__ __forceinline__ void load_box_window(const float* row, float (&w)[kSsimWin]) {
+  const float4* r4 = reinterpret_cast<const float4*>(row);
+  float v[24];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) {
+    const float4 q = r4[k];
+    v[4 * k] = q.x;
+    v[4 * k + 1] = q.y;
+    v[4 * k + 2] = q.z;
+    v[4 * k + 3] = q.w;
+  }
+#pragma unroll
+  for (int k = 0; k < kSsimWin; ++k) w[k] = v[k + kSsimBoxOff];
+}
+
 __device__ __forceinline__ void store_run(float* dst, const float (&v)[kSsimRun]) {
   float4* d4 = reinterpret_cast<float4*>(dst);  // 16-byte aligned: offsets of 8 floats
 #pragma unroll
@@ -85,20 +114,22 @@ __device__ __forceinline__ void store_run(float* dst, const float (&v)[kSsimRun]
     d4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
 }
 
-// Derivative maps are planar: maps[(3 * kind + channel) * H * W + pixel], kind A, B, Cm; they
-// are zero outside the interior (positions whose window leaves the image), so the backward's
-// blurs of them only gather from interior positions.
+// Derivative maps are planar, channel-major: maps[(3 * channel + kind) * H * pitch + y * pitch
+// + x], kind A, B, Cm, with the row pitch W rounded up to a multiple of 4 floats (so a tile copy
+// can address them, and a channel's three planes are one box); they are zero outside the
+// interior (positions whose window leaves the image), so the backward's blurs of them only
+// gather from interior positions.
 __device__ __forceinline__ float clamp01(float v) { return fminf(fmaxf(v, 0.f), 1.f); }
 
 __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
-    int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
+    int H, int W, int pitch, const float* __restrict__ img, const float* __restrict__ ref,
     float* __restrict__ maps, double* __restrict__ partials) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   SsimForwardSmem& s = *reinterpret_cast<SsimForwardSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bx = blockIdx.x * kSsimTW, by = blockIdx.y * kSsimTH;
   const int x0 = bx - kSsimR, y0 = by - kSsimR;
-  const size_t HW = (size_t)H * W;
+  const size_t plane = (size_t)H * pitch;
   // this thread's vertical run: column col, output rows [rb * 8, rb * 8 + 8)
   const int rb = tid / kSsimTW, col = tid % kSsimTW;
   const int gx = bx + col;
@@ -116,15 +147,16 @@ __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
         for (int rr = 0; rr < kBatch; ++rr) {
           const int py = warp + (r0 + rr) * kSsimWarps, gy = y0 + py;
           const bool row_ok = r0 + rr < kRowsPerWarp && py < kSsimInH && gy >= 0 && gy < H;
+          // channel c of the row; the lanes index it with 32-bit offsets
+          const size_t row_off = row_ok ? (size_t)gy * W * 3 + c : 0;
+          const float* irow = img + row_off;
+          const float* rrow = ref + row_off;
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int px = lane + 32 * u, gxx = x0 + px;
-            a[rr][u] = b[rr][u] = 0.f;
-            if (row_ok && px < kSsimInW && gxx >= 0 && gxx < W) {
-              const size_t o = ((size_t)gy * W + gxx) * 3 + c;
-              a[rr][u] = clamp01(__ldg(img + o));
-              b[rr][u] = clamp01(__ldg(ref + o));
-            }
+            const bool ok = row_ok && px < kSsimInW && (unsigned)gxx < (unsigned)W;
+            a[rr][u] = ok ? clamp01(__ldg(irow + 3 * gxx)) : 0.f;
+            b[rr][u] = ok ? clamp01(__ldg(rrow + 3 * gxx)) : 0.f;
           }
         }
 #pragma unroll
@@ -201,9 +233,10 @@ __global__ void __launch_bounds__(kSsimThreads, 5) ssim_forward_kernel(
           A = dmx - 2.f * mx * B - my * Cm;
           run_ssim += S;
         }
-        maps[(0 + c) * HW + pix] = A;
-        maps[(3 + c) * HW + pix] = B;
-        maps[(6 + c) * HW + pix] = Cm;
+        const size_t mp = (size_t)(3 * c) * plane + (size_t)gy * pitch + gx;
+        maps[mp] = A;
+        maps[mp + plane] = B;
+        maps[mp + 2 * plane] = Cm;
         const size_t p3 = pix * 3 + c;
         run_l1 += fabsf(__ldg(img + p3) - __ldg(ref + p3));
       }
@@ -263,67 +296,73 @@ __global__ void __launch_bounds__(256) ssim_finalize_kernel(const double* __rest
   }
 }
 
-__global__ void __launch_bounds__(kSsimThreads, 6) ssim_backward_kernel(
-    int H, int W, const float* __restrict__ img, const float* __restrict__ ref,
-    const float* __restrict__ maps, const float* __restrict__ grad_loss, float lambda,
-    float inv_n_l1, float inv_n_ssim, float* __restrict__ grad_img) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+// Backward, one channel at a time: the channel's A, B, Cm planes over the tile and its 5-pixel
+// halo arrive in s.m (columns bx - 8 .. bx + 39: the copy's start column must be a multiple of
+// 4 floats, so the halo's first column sits at offset kSsimBoxOff), are blurred horizontally
+// into s.h, then vertically per thread run, and combined with x, y and sign(x - y). kTma: one
+// tensor-memory-accelerator copy of the three planes per channel (they are adjacent in the map
+// layout), issued by thread 0 as soon as the previous channel's horizontal pass has read s.m,
+// so it overlaps that channel's vertical pass; otherwise the warps load the planes themselves.
+template <bool kTma>
+__global__ void __launch_bounds__(kSsimThreads, 5) ssim_backward_kernel(
+    int H, int W, int pitch, const float* __restrict__ img, const float* __restrict__ ref,
+    const float* __restrict__ maps, const __grid_constant__ CUtensorMap map_desc,
+    const float* __restrict__ grad_loss, float lambda, float inv_n_l1, float inv_n_ssim,
+    float* __restrict__ grad_img) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   SsimBackwardSmem& s = *reinterpret_cast<SsimBackwardSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bx = blockIdx.x * kSsimTW, by = blockIdx.y * kSsimTH;
-  const int x0 = bx - kSsimR, y0 = by - kSsimR;
-  const size_t HW = (size_t)H * W;
+  const int x0 = bx - kSsimBoxOff - kSsimR, y0 = by - kSsimR;  // box origin
+  const size_t plane = (size_t)H * pitch;
   const float g = __ldg(grad_loss);
   const float w_l1 = g * (1.0f - lambda) * inv_n_l1, w_ssim = -g * lambda * inv_n_ssim;
   const int rb = tid / kSsimTW, col = tid % kSsimTW;
   const int gx = bx + col;
+  bool copies_ok = true;
+  if (kTma) {
+    if (tid == 0) {
+      mbar_init(&s.bar, 1);
+      mbar_arrive_expect_tx(&s.bar, kSsimBoxBytes);
+      tma_load_3d(&s.m[0][0][0], &map_desc, x0, y0, 0, &s.bar);
+    }
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+  }
 #pragma unroll 1
   for (int c = 0; c < 3; ++c) {
-    // planes A_c, B_c, Cm_c: one warp per halo row, 8 rows in flight per warp
-    {
-      constexpr int kRows = 3 * kSsimInH;
-      constexpr int kRowsPerWarp = (kRows + kSsimWarps - 1) / kSsimWarps;
-      constexpr int kBatch = 8;
+    if (kTma) {
+      if (!mbar_wait(&s.bar, (unsigned)(c & 1), kCopyWaitNs)) copies_ok = false;
+    } else {
+      // planes A_c, B_c, Cm_c: one warp per halo row, lanes along it (48 columns)
+      const float* chan = maps + (size_t)(3 * c) * plane;
 #pragma unroll 1
-      for (int r0 = 0; r0 < kRowsPerWarp; r0 += kBatch) {
-        float v[kBatch][2];
+      for (int row = warp; row < 3 * kSsimInH; row += kSsimWarps) {
+        const int kind = row / kSsimInH, py = row - kind * kSsimInH, gy = y0 + py;
+        const float* src = chan + (size_t)kind * plane + (size_t)gy * pitch;
 #pragma unroll
-        for (int rr = 0; rr < kBatch; ++rr) {
-          const int row = warp + (r0 + rr) * kSsimWarps;
-          const int kind = row / kSsimInH, py = row - kind * kSsimInH, gy = y0 + py;
-          const bool row_ok = r0 + rr < kRowsPerWarp && row < kRows && gy >= 0 && gy < H;
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int px = lane + 32 * u, gxx = x0 + px;
-            v[rr][u] = (row_ok && px < kSsimInW && gxx >= 0 && gxx < W)
-                           ? __ldg(maps + (3 * kind + c) * HW + (size_t)gy * W + gxx)
-                           : 0.f;
-          }
-        }
-#pragma unroll
-        for (int rr = 0; rr < kBatch; ++rr) {
-          const int row = warp + (r0 + rr) * kSsimWarps;
-          if (r0 + rr >= kRowsPerWarp || row >= kRows) break;
-          const int kind = row / kSsimInH, py = row - kind * kSsimInH;
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int px = lane + 32 * u;
-            if (px < kSsimInW) s.m[kind][py][px] = v[rr][u];
-          }
+        for (int u = 0; u < 2; ++u) {
+          const int px = lane + 32 * u, gxx = x0 + px;
+          if (px < kSsimBoxW)
+            s.m[kind][py][px] = (gy >= 0 && gy < H && gxx >= 0 && gxx < W) ? __ldg(src + gxx)
+                                                                           : 0.f;
         }
       }
+      __syncthreads();
     }
-    __syncthreads();
     for (int it = tid; it < 3 * kSsimInH * (kSsimTW / kSsimRun); it += kSsimThreads) {
       const int kind = it / (kSsimInH * (kSsimTW / kSsimRun));
       const int rem = it - kind * (kSsimInH * (kSsimTW / kSsimRun));
       const int r = rem / (kSsimTW / kSsimRun), cb = rem - r * (kSsimTW / kSsimRun);
       float w[kSsimWin], out[kSsimRun];
-      load_row_window(&s.m[kind][r][cb * kSsimRun], w);
+      load_box_window(&s.m[kind][r][cb * kSsimRun], w);
       blur_run(w, out);
       store_run(&s.h[kind][r][cb * kSsimRun], out);
     }
     __syncthreads();
+    if (kTma && tid == 0 && c < 2) {  // s.m is free: the next channel's planes
+      mbar_arrive_expect_tx(&s.bar, kSsimBoxBytes);
+      tma_load_3d(&s.m[0][0][0], &map_desc, x0, y0, 3 * (c + 1), &s.bar);
+    }
     float bl[3][kSsimRun];
 #pragma unroll
     for (int kind = 0; kind < 3; ++kind) {
@@ -347,7 +386,12 @@ __global__ void __launch_bounds__(kSsimThreads, 6) ssim_backward_kernel(
                            : 0.f;
       grad_img[p] = w_l1 * sgn + gs;
     }
-    __syncthreads();  // the next channel overwrites the planes
+    __syncthreads();  // the next channel overwrites s.h (and, without kTma, s.m)
+  }
+  if (kTma && !copies_ok) {
+    raise_device_error(kErrCopyTimeout);
+    // no copy may still be landing in this CTA's shared memory when it exits
+    if (tid == 0) mbar_wait(&s.bar, 0u, kCopyWaitNs);
   }
 }
 
@@ -375,13 +419,27 @@ static size_t ssim_blocks(int H, int W) {
   return (size_t)((W + kSsimTW - 1) / kSsimTW) * ((H + kSsimTH - 1) / kSsimTH);
 }
 
+// Workspace: the derivative maps (row pitch W rounded up to 4 floats) from the first 256-byte
+// boundary, then the per-block partial sums.
+static int map_pitch(int W) { return (W + 3) & ~3; }
+static size_t maps_bytes(int H, int W) { return (size_t)H * map_pitch(W) * 9 * sizeof(float); }
+static float* maps_of(const void* workspace) {
+  return reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255u) &
+                                  ~uintptr_t(255u));
+}
+static double* partials_of(const void* workspace, int H, int W) {
+  return reinterpret_cast<double*>(
+      (reinterpret_cast<uintptr_t>(maps_of(workspace)) + maps_bytes(H, W) + 255u) &
+      ~uintptr_t(255u));
+}
+
 }  // namespace gs
 
 using namespace gs;
 
 extern "C" size_t gs_l1_ssim_workspace_size(int H, int W) {
   if (H <= 0 || W <= 0) return 0;
-  return (size_t)H * W * 9 * sizeof(float) + ssim_blocks(H, W) * 2 * sizeof(double) + 256;
+  return 256 + maps_bytes(H, W) + 256 + ssim_blocks(H, W) * 2 * sizeof(double);
 }
 
 static double ssim_count(int H, int W) { return 3.0 * (H - 2 * kSsimR) * (W - 2 * kSsimR); }
@@ -396,15 +454,15 @@ extern "C" int gs_l1_ssim_forward(int H, int W, const float* img, const float* t
   GS_REQUIRE(workspace_bytes >= gs_l1_ssim_workspace_size(H, W), "workspace too small");
   const int rc = ensure_gauss();
   if (rc != GS_OK) return rc;
-  float* maps = static_cast<float*>(workspace);
-  double* partials = reinterpret_cast<double*>(
-      (reinterpret_cast<uintptr_t>(maps + (size_t)H * W * 9) + 255u) & ~uintptr_t(255u));
+  float* maps = maps_of(workspace);
+  double* partials = partials_of(workspace, H, W);
   const dim3 grid((W + kSsimTW - 1) / kSsimTW, (H + kSsimTH - 1) / kSsimTH);
   const size_t smem = sizeof(SsimForwardSmem);
   GS_CUDA(cudaFuncSetAttribute(ssim_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
   cudaStream_t st = (cudaStream_t)stream;
-  ssim_forward_kernel<<<grid, kSsimThreads, smem, st>>>(H, W, img, target, maps, partials);
+  ssim_forward_kernel<<<grid, kSsimThreads, smem, st>>>(H, W, map_pitch(W), img, target, maps,
+                                                        partials);
   GS_CHECK_LAUNCH();
   ssim_finalize_kernel<<<1, 256, 0, st>>>(partials, (int)(grid.x * grid.y), ssim_count(H, W),
                                           (double)H * W * 3, lambda_dssim, loss, ssim_value);
@@ -426,11 +484,29 @@ extern "C" int gs_l1_ssim_backward(int H, int W, const float* img, const float* 
   if (rc != GS_OK) return rc;
   const dim3 grid((W + kSsimTW - 1) / kSsimTW, (H + kSsimTH - 1) / kSsimTH);
   const size_t smem = sizeof(SsimBackwardSmem);
-  GS_CUDA(cudaFuncSetAttribute(ssim_backward_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ssim_backward_kernel<<<grid, kSsimThreads, smem, (cudaStream_t)stream>>>(
-      H, W, img, target, static_cast<const float*>(workspace), grad_loss, lambda_dssim,
-      (float)(1.0 / ((double)H * W * 3)), (float)(1.0 / ssim_count(H, W)), grad_img);
+  const float* maps = maps_of(workspace);
+  const int pitch = map_pitch(W);
+  // the channel's three planes as one tile copy where the driver can describe them
+  CUtensorMap desc;
+  std::memset(&desc, 0, sizeof(desc));
+  const bool tma = encode_f32_3d(&desc, maps, (uint64_t)W, (uint64_t)H, 9, (uint64_t)pitch,
+                                 (uint64_t)H * pitch, kSsimBoxW, kSsimInH, 3);
+  const float inv_n_l1 = (float)(1.0 / ((double)H * W * 3));
+  const float inv_n_ssim = (float)(1.0 / ssim_count(H, W));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (tma) {
+    GS_CUDA(cudaFuncSetAttribute(ssim_backward_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ssim_backward_kernel<true><<<grid, kSsimThreads, smem, st>>>(
+        H, W, pitch, img, target, maps, desc, grad_loss, lambda_dssim, inv_n_l1, inv_n_ssim,
+        grad_img);
+  } else {
+    GS_CUDA(cudaFuncSetAttribute(ssim_backward_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ssim_backward_kernel<false><<<grid, kSsimThreads, smem, st>>>(
+        H, W, pitch, img, target, maps, desc, grad_loss, lambda_dssim, inv_n_l1, inv_n_ssim,
+        grad_img);
+  }
   GS_CHECK_LAUNCH();
   return GS_OK;
   GS_API_END();

@@ -397,7 +397,8 @@ GS_API unsigned long long gs_kernel_launches(void);
  * Device-side error bits recorded by the kernels of earlier calls on this device since
  * the last gs_clear_device_errors() (1 = a look-back wait gave up, 2 = pair capacity
  * exceeded, 4 = an index out of range, 8 = a cross-GPU barrier wait of gs_sharded_adam_step
- * gave up). Synchronises the device.
+ * gave up, 16 = a wait for a tile copy of the tensor memory accelerator gave up).
+ * Synchronises the device.
  */
 GS_API int gs_device_error_bits(unsigned* bits);
 GS_API int gs_clear_device_errors(void);
