@@ -695,7 +695,7 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-render-table", action="store_true",
                     help="skip the per-scene forward/backward/FPS table (configs 1-3)")
-    ap.add_argument("--view-streams", type=int, default=6,
+    ap.add_argument("--view-streams", type=int, default=8,
                     help="CUDA streams the views of a step alternate over (1 = in order)")
     ap.add_argument("--view-only", action="store_true",
                     help="forward+backward of one config-2 view per step (single GPU); a small "

@@ -199,7 +199,7 @@ class Trainer:
 
     def __init__(self, scene, views, targets, device, rank=0, world=1, group=None,
                  fused_adam: bool = True, fused_loss: bool = True, mode: str = "direct",
-                 view_streams: int = 6, tight_bins: bool = True,
+                 view_streams: int = 8, tight_bins: bool = True,
                  param_clamps: dict | None = None, combined_backward: bool = True):
         from gaussian_splatting.scene.gaussian import gaussian
 
