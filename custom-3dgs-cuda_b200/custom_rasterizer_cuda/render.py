@@ -204,10 +204,14 @@ def render_backward(state: RenderState, grad_img, mu, q, s, albedo, k_j, R, t, c
     return (*out, g_mean2d)
 
 
+def backward_workspace_bytes(n: int) -> int:
+    """Bytes of one view's render_backward_blend workspace for n Gaussians."""
+    return int(lib.gs_render_backward_workspace_size(int(n)))
+
+
 def backward_workspace(n: int, device) -> torch.Tensor:
     """A workspace for one view's render_backward_blend sums (3 float4 per Gaussian)."""
-    return torch.empty((lib.gs_render_backward_workspace_size(int(n)),), device=device,
-                       dtype=torch.uint8)
+    return torch.empty((backward_workspace_bytes(n),), device=device, dtype=torch.uint8)
 
 
 def render_backward_blend(state: RenderState, grad_img, n: int, workspace=None) -> torch.Tensor:

@@ -338,10 +338,14 @@ class Trainer:
             combined = self.combined_backward
             if combined:
                 from custom_rasterizer_cuda.render import (backward_workspace,
+                                                           backward_workspace_bytes,
                                                            render_backward_blend,
                                                            render_backward_views)
+                n_g = g.mu.shape[0]
+                self._sums = [ws if ws.numel() >= backward_workspace_bytes(n_g) else
+                              backward_workspace(n_g, self.device) for ws in self._sums]
                 while len(self._sums) < len(views):
-                    self._sums.append(backward_workspace(g.mu.shape[0], self.device))
+                    self._sums.append(backward_workspace(n_g, self.device))
 
             def render_view(k, vi, st, done, prev_done, capacity=None, accumulate=None):
                 v = self.views[vi]
