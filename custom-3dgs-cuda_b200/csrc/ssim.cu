@@ -24,6 +24,7 @@
 // Backward: the same tiling, a channel at a time, blurs A, B, Cm and combines them with x,
 // y and sign(x - y). One channel's planes (41 KB / 37 KB of shared memory) leave room for 5-6
 // CTAs per SM.
+#include <cstdlib>
 #include <cstring>
 
 #include "capi_internal.h"
@@ -486,10 +487,13 @@ extern "C" int gs_l1_ssim_backward(int H, int W, const float* img, const float* 
   const size_t smem = sizeof(SsimBackwardSmem);
   const float* maps = maps_of(workspace);
   const int pitch = map_pitch(W);
-  // the channel's three planes as one tile copy where the driver can describe them
+  // the channel's three planes as one tile copy where the driver can describe them;
+  // GS3D_SSIM_NO_TMA=1 selects the warps' own loads (same results), which tests compare
   CUtensorMap desc;
   std::memset(&desc, 0, sizeof(desc));
-  const bool tma = encode_f32_3d(&desc, maps, (uint64_t)W, (uint64_t)H, 9, (uint64_t)pitch,
+  const char* no_tma = std::getenv("GS3D_SSIM_NO_TMA");
+  const bool tma = !(no_tma && no_tma[0] == '1') &&
+                   encode_f32_3d(&desc, maps, (uint64_t)W, (uint64_t)H, 9, (uint64_t)pitch,
                                  (uint64_t)H * pitch, kSsimBoxW, kSsimInH, 3);
   const float inv_n_l1 = (float)(1.0 / ((double)H * W * 3));
   const float inv_n_ssim = (float)(1.0 / ssim_count(H, W));

@@ -116,3 +116,19 @@ def test_fused_l1_ssim_rejects_images_below_the_window(cuda_device):
     a = torch.rand(10, 64, 3, device=cuda_device)
     with pytest.raises(RuntimeError, match="at least 11 x 11"):
         l1_ssim_loss(a, a.clone())
+
+
+@pytest.mark.parametrize("shape", [(1080, 1920), (37, 53)])
+def test_ssim_backward_tile_copies_match_warp_loads(cuda_device, shape, monkeypatch):
+    """The SSIM backward reads its derivative-map planes through tile copies of the tensor
+    memory accelerator; its fallback (the warps' own loads, for a driver without the
+    tensor-map entry point) must give the same bits."""
+    from gs3d_b200.loss import l1_ssim_value_and_grad
+
+    H, W = shape
+    img, target = _pair(H, W, 31 + H, spill=True)
+    x, y = img.to(cuda_device), target.to(cuda_device)
+    loss_a, grad_a = l1_ssim_value_and_grad(x, y, 0.2)
+    monkeypatch.setenv("GS3D_SSIM_NO_TMA", "1")
+    loss_b, grad_b = l1_ssim_value_and_grad(x, y, 0.2)
+    assert torch.equal(loss_a, loss_b) and torch.equal(grad_a, grad_b)
