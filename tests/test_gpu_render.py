@@ -228,6 +228,15 @@ def test_combined_per_gaussian_backward_over_views(cuda_device):
     for a, b, c in zip(out_all + st_all, out_one + st_one, out_two + st_two):
         assert torch.equal(a, b) and torch.equal(a, c)
     assert int((st_all[1] > 0).sum()) > N // 2  # most Gaussians are seen by some view
+    # more entries than one launch takes (GS_MAX_VIEWS_PER_CALL = 16): two launches, same bits
+    many = [entries[k % len(entries)] for k in range(18)]
+    out_many, st_many = fresh()
+    render_backward_views(many, mu, q, s, A, kj, out_many, stats=st_many)
+    out_seq, st_seq = fresh()
+    for k, e in enumerate(many):
+        render_backward_views([e], mu, q, s, A, kj, out_seq, accumulate=k > 0, stats=st_seq)
+    for a, b in zip(out_many + st_many, out_seq + st_seq):
+        assert torch.equal(a, b)
 
     # against render_backward per view (its own blend pass: the same sums up to atomic order)
     out_ref, st_ref = fresh()
