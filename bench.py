@@ -612,6 +612,29 @@ def cpu_baseline_sample(scene, view, target, adam_seconds: float | None = None) 
                       "all parameters (the step's optimizer work per view)"}
 
 
+def torch_cpu_config0(table: dict | None) -> dict:
+    """BASELINE config 0's step (4,096 Gaussians at 128x128: forward, then the backward of L1
+    against a seeded target) by the vectorised PyTorch restatement on the host cores, beside the
+    same step on the GPU through RasterizeFunction (the render table's config-0 row)."""
+    from gs3d_b200 import scenes
+    from oracle import torch_cpu
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sc = scenes.config0(0)
+    view = sc.views[0]
+    target = torch.rand(view.height, view.width, 3, generator=torch.Generator().manual_seed(1))
+    seconds, threads = torch_cpu.step_seconds(sc, view, target)
+    out = {"value": 1.0 / seconds, "unit": "config-0 steps/s", "cores": threads,
+           "kind": "torch-cpu restatement (oracle/torch_cpu.py)",
+           "sample": "config 0: 4,096 Gaussians, 128x128, forward + L1 backward, median of 3"}
+    row = (table or {}).get("config0_4096_128x128")
+    if row:
+        gpu_ms = row["fwd_ms"] + row["bwd_ms"]
+        out["gpu_same_step_ms"] = gpu_ms
+        out["gpu_over_cpu"] = seconds * 1e3 / gpu_ms
+    return out
+
+
 def cpu_adam_seconds(scene) -> float:
     """Seconds of one torch.optim.Adam step (eps 1e-15, the step's learning rates) over all
     parameters on the host cores."""
@@ -925,6 +948,7 @@ def run_ours(args, rank, world, local) -> int:
         line["cpu_baseline"] = cpu_baseline_sample(sc, sc.views[0], targets[0],
                                                    cpu_adam_seconds(sc))
         line["cpu_baseline"].pop("seconds", None)
+        line["cpu_baseline_torch"] = torch_cpu_config0(line.get("render_table"))
     emit(line)
     return 0
 
