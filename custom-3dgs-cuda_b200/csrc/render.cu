@@ -645,6 +645,8 @@ extern "C" int gs_render_backward_gaussians(int N, int n_views, const gs_view_su
   for (int v = 0; v < n_views; ++v) {
     const gs_view_sums& w = views[v];
     GS_REQUIRE(w.workspace && w.R && w.t && w.cam_pos, "null pointer in a view");
+    GS_REQUIRE(w.workspace_bytes >= gs_render_backward_workspace_size(N),
+               "a view's workspace is smaller than gs_render_backward_workspace_size(N)");
     p.views[v] = w;
     p.accum[v] = blend_sums(const_cast<void*>(w.workspace));
   }

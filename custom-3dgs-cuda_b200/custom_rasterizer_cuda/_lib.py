@@ -85,7 +85,8 @@ class ViewSums(ctypes.Structure):
     """Mirror of gs_view_sums (include/gs3d_b200.h): one view's blend-backward workspace and
     camera for gs_render_backward_gaussians."""
 
-    _fields_ = [("workspace", c_void_p), ("R", c_void_p), ("t", c_void_p), ("cam_pos", c_void_p),
+    _fields_ = [("workspace", c_void_p), ("workspace_bytes", c_size_t), ("R", c_void_p),
+                ("t", c_void_p), ("cam_pos", c_void_p),
                 ("fx", c_float), ("fy", c_float), ("cx", c_float), ("cy", c_float),
                 ("stat_scale_x", c_float), ("stat_scale_y", c_float)]
 

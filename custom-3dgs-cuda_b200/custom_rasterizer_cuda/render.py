@@ -249,8 +249,9 @@ def render_backward_views(views, mu, q, s, albedo, k_j, out, accumulate: bool = 
             chunk = views[c0:c0 + GS_MAX_VIEWS_PER_CALL]
             arr = (ViewSums * len(chunk))()
             for k, (ws, R, t, cam, fx, fy, cx, cy, sx, sy) in enumerate(chunk):
-                arr[k] = ViewSums(ws.data_ptr(), _ptr(R), _ptr(t), _ptr(cam), float(fx),
-                                  float(fy), float(cx), float(cy), float(sx), float(sy))
+                arr[k] = ViewSums(ws.data_ptr(), ws.numel() * ws.element_size(), _ptr(R),
+                                  _ptr(t), _ptr(cam), float(fx), float(fy), float(cx),
+                                  float(cy), float(sx), float(sy))
             check(lib.gs_render_backward_gaussians(
                 N, len(chunk), ctypes.addressof(arr), _ptr(mu), _ptr(q), _ptr(s), _ptr(albedo),
                 _ptr(k_j), *(_ptr(o) for o in out), 1 if (accumulate or c0 > 0) else 0, *st,

@@ -218,6 +218,7 @@ GS_API int gs_render_backward(int N, int H, int W, const float* grad_img, const 
 #define GS_MAX_VIEWS_PER_CALL 16
 typedef struct gs_view_sums {
   const void* workspace;  /* the view's gs_render_backward_blend workspace */
+  size_t workspace_bytes; /* its size, at least gs_render_backward_workspace_size(N) */
   const float* R;         /* [3, 3] device, the view's camera as in gs_render_forward */
   const float* t;         /* [3] device */
   const float* cam_pos;   /* [3] device */

@@ -237,6 +237,10 @@ def test_combined_per_gaussian_backward_over_views(cuda_device):
         render_backward_views([e], mu, q, s, A, kj, out_seq, accumulate=k > 0, stats=st_seq)
     for a, b in zip(out_many + st_many, out_seq + st_seq):
         assert torch.equal(a, b)
+    # a workspace smaller than one view's sums is refused before any GPU work
+    small = (entries[0][0][:1024],) + tuple(entries[0][1:])
+    with pytest.raises(RuntimeError, match="smaller than gs_render_backward_workspace_size"):
+        render_backward_views([small], mu, q, s, A, kj, fresh()[0])
 
     # against render_backward per view (its own blend pass: the same sums up to atomic order)
     out_ref, st_ref = fresh()
