@@ -199,11 +199,18 @@ struct DupParams {
 
 // Exclusive scan of the tile counts in depth order and duplication of each Gaussian into
 // one (tile id, Gaussian index) pair per covered tile, row-major over its rectangle
-// (the order of csrc/forward/rasterize.cu:124-135). A warp's 32 Gaussians own a contiguous run
-// of pairs, which the warp writes 32 at a time: lanes where a Gaussian's pairs start in the
-// current window record their lane in a per-warp table and the window's start positions are
-// OR-reduced into one mask; pair lane q takes the Gaussian of the highest start at or below q
-// (or the one carried from the previous window) and fetches its rectangle by shuffle.
+// (the order of csrc/forward/rasterize.cu:124-135). A CTA takes kDupRuns consecutive runs of
+// kBinThreads Gaussians: one look-back per CTA over a quarter as many CTAs as runs keeps the
+// decoupled look-back chain short (with one run per CTA the other warps spent most of the
+// kernel waiting at the barrier behind warp 0's walk), and the runs' rectangle loads are in
+// flight together. Within a run a warp's 32 Gaussians own a contiguous run of pairs, which the
+// warp writes 32 at a time: lanes where a Gaussian's pairs start in the current window record
+// their lane in a per-warp table and the window's start positions are OR-reduced into one
+// mask; pair lane q takes the Gaussian of the highest start at or below q (or the one carried
+// from the previous window) and fetches its rectangle by shuffle.
+constexpr int kDupRuns = 4;
+constexpr int kDupItems = kBinThreads * kDupRuns;  // Gaussians per CTA
+
 static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p) {
   __shared__ unsigned s_tile, s_prefix;
   __shared__ unsigned s_scan[33];
@@ -213,22 +220,32 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
   constexpr unsigned kFull = 0xffffffffu;
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int nv = *p.n_visible;
-  const int num_tiles = (nv + kBinThreads - 1) / kBinThreads;
+  const int num_tiles = (nv + kDupItems - 1) / kDupItems;
   if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
   for (int k = tid; k < 4 * 256; k += kBinThreads) (&s_hist[0][0])[k] = 0u;
   __syncthreads();
   const int tile = (int)s_tile;
   if (tile >= num_tiles) return;
-  const int j = tile * kBinThreads + tid;
-  unsigned count = 0, gid = 0;
-  uint2 pr = make_uint2(0u, 0u);
-  if (j < nv) {
-    gid = p.sorted_gids[j];
-    pr = p.rects[gid];
-    count = rect_count(unpack_rect(pr));
+  unsigned count[kDupRuns], gid[kDupRuns];
+  uint2 pr[kDupRuns];
+#pragma unroll
+  for (int r = 0; r < kDupRuns; ++r) {
+    const int j = tile * kDupItems + r * kBinThreads + tid;
+    gid[r] = j < nv ? p.sorted_gids[j] : 0u;
   }
-  unsigned tile_pairs;
-  const unsigned excl = block_exclusive_scan(count, s_scan, &tile_pairs);
+#pragma unroll
+  for (int r = 0; r < kDupRuns; ++r) {
+    const int j = tile * kDupItems + r * kBinThreads + tid;
+    pr[r] = j < nv ? p.rects[gid[r]] : make_uint2(0u, 0u);
+    count[r] = j < nv ? rect_count(unpack_rect(pr[r])) : 0u;
+  }
+  // per run: each thread's exclusive offset within its run, and the run's total
+  unsigned excl[kDupRuns], run_pairs[kDupRuns], tile_pairs = 0;
+#pragma unroll
+  for (int r = 0; r < kDupRuns; ++r) {
+    excl[r] = block_exclusive_scan(count[r], s_scan, &run_pairs[r]);
+    tile_pairs += run_pairs[r];
+  }
   if (tid == 0)
     st_relaxed(p.status + tile, (tile == 0 ? kFlagPrefix : kFlagAggregate) | tile_pairs);
   if (tid < 32) {
@@ -240,54 +257,60 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
     }
   }
   __syncthreads();
-  const unsigned base = s_prefix;
   const unsigned M = (unsigned)*p.pair_count;
-  if (base + tile_pairs > M) {  // only reachable after a look-back timeout
+  if (s_prefix + tile_pairs > M) {  // only reachable after a look-back timeout
     if (tid == 0) raise_device_error(kErrBadIndex);
     return;
   }
-  // this warp's run of pairs: [w_first, w_first + w_total) of the block's
-  const unsigned w_first = __shfl_sync(kFull, excl, 0);
-  const unsigned w_total = __shfl_sync(kFull, excl + count, 31) - w_first;
-  const unsigned my_o = excl - w_first;
-  const TileRect mine = unpack_rect(pr);
-  const unsigned my_w = count > 0 ? (unsigned)(mine.x1 - mine.x0) : 1u;
-  const float my_inv_w = 1.0f / (float)my_w;
-  unsigned* table = s_owner[warp];
   const unsigned le = lane == 31 ? kFull : ((2u << lane) - 1u);  // lanes 0..lane
-  int carried = 0;
-  for (unsigned wb = 0; wb < w_total; wb += 32) {
-    const bool starts_here = count > 0 && my_o >= wb && my_o < wb + 32;
-    if (starts_here) table[my_o - wb] = (unsigned)lane;
-    const unsigned starts = __reduce_or_sync(kFull, starts_here ? 1u << (my_o - wb) : 0u);
-    __syncwarp();
-    const unsigned m = starts & le;
-    const int owner = m ? (int)table[31 - __clz(m)] : carried;
-    const unsigned o_own = __shfl_sync(kFull, my_o, owner);
-    const unsigned rx = __shfl_sync(kFull, pr.x, owner), ry = __shfl_sync(kFull, pr.y, owner);
-    const unsigned g_own = __shfl_sync(kFull, gid, owner);
-    const float inv_w = __shfl_sync(kFull, my_inv_w, owner);
-    const unsigned q = wb + (unsigned)lane;
-    if (q < w_total) {
-      const TileRect r = unpack_rect(make_uint2(rx, ry));
-      const unsigned w = (unsigned)(r.x1 - r.x0);
-      const unsigned lp = q - o_own;
-      // row = lp / w from the float reciprocal, then made exact
-      unsigned row = (unsigned)(((float)lp + 0.5f) * inv_w);
-      if (row * w > lp) --row;
-      if ((row + 1) * w <= lp) ++row;
-      const unsigned col = lp - row * w;
-      const unsigned tile_id =
-          (unsigned)(r.y0 + (int)row) * (unsigned)p.tiles_x + (unsigned)r.x0 + col;
-      p.tile_keys[base + w_first + q] = tile_id;
-      p.tile_vals[base + w_first + q] = g_own;
+  unsigned* table = s_owner[warp];
+  unsigned base = s_prefix;  // first pair of the current run
 #pragma unroll
-      for (int pass = 0; pass < 4; ++pass)  // constant indices keep the parameters in registers
-        if (pass < p.n_tile_passes)
-          atomicAdd(&s_hist[pass][(tile_id >> p.tile_shift[pass]) & p.tile_mask[pass]], 1u);
+  for (int r = 0; r < kDupRuns; ++r) {
+    // this warp's run of pairs: [w_first, w_first + w_total) of the run's
+    const unsigned w_first = __shfl_sync(kFull, excl[r], 0);
+    const unsigned w_total = __shfl_sync(kFull, excl[r] + count[r], 31) - w_first;
+    const unsigned my_o = excl[r] - w_first;
+    const TileRect mine = unpack_rect(pr[r]);
+    const unsigned my_w = count[r] > 0 ? (unsigned)(mine.x1 - mine.x0) : 1u;
+    const float my_inv_w = 1.0f / (float)my_w;
+    const bool has = count[r] > 0;
+    const unsigned prx = pr[r].x, pry = pr[r].y, my_gid = gid[r];
+    int carried = 0;
+    for (unsigned wb = 0; wb < w_total; wb += 32) {
+      const bool starts_here = has && my_o >= wb && my_o < wb + 32;
+      if (starts_here) table[my_o - wb] = (unsigned)lane;
+      const unsigned starts = __reduce_or_sync(kFull, starts_here ? 1u << (my_o - wb) : 0u);
+      __syncwarp();
+      const unsigned m = starts & le;
+      const int owner = m ? (int)table[31 - __clz(m)] : carried;
+      const unsigned o_own = __shfl_sync(kFull, my_o, owner);
+      const unsigned rx = __shfl_sync(kFull, prx, owner), ry = __shfl_sync(kFull, pry, owner);
+      const unsigned g_own = __shfl_sync(kFull, my_gid, owner);
+      const float inv_w = __shfl_sync(kFull, my_inv_w, owner);
+      const unsigned q = wb + (unsigned)lane;
+      if (q < w_total) {
+        const TileRect rc = unpack_rect(make_uint2(rx, ry));
+        const unsigned w = (unsigned)(rc.x1 - rc.x0);
+        const unsigned lp = q - o_own;
+        // row = lp / w from the float reciprocal, then made exact
+        unsigned row = (unsigned)(((float)lp + 0.5f) * inv_w);
+        if (row * w > lp) --row;
+        if ((row + 1) * w <= lp) ++row;
+        const unsigned col = lp - row * w;
+        const unsigned tile_id =
+            (unsigned)(rc.y0 + (int)row) * (unsigned)p.tiles_x + (unsigned)rc.x0 + col;
+        p.tile_keys[base + w_first + q] = tile_id;
+        p.tile_vals[base + w_first + q] = g_own;
+#pragma unroll
+        for (int pass = 0; pass < 4; ++pass)  // constant indices keep the parameters in registers
+          if (pass < p.n_tile_passes)
+            atomicAdd(&s_hist[pass][(tile_id >> p.tile_shift[pass]) & p.tile_mask[pass]], 1u);
+      }
+      carried = __shfl_sync(kFull, owner, 31);
+      __syncwarp();  // the next window rewrites the table
     }
-    carried = __shfl_sync(kFull, owner, 31);
-    __syncwarp();  // the next window rewrites the table
+    base += run_pairs[r];
   }
   __syncthreads();
   for (int k = tid; k < p.n_tile_passes * 256; k += kBinThreads) {

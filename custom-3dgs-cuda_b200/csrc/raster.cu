@@ -182,7 +182,8 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
     dp.tile_keys = tk[0];
     dp.tile_vals = tv[0];
     dp.tile_hist = reinterpret_cast<unsigned*>(ws + L.tile_hist);
-    scan_duplicate_kernel<<<(unsigned)L.nb, kBinThreads, 0, stream>>>(dp);
+    const unsigned dup_blocks = (unsigned)(((long long)N + kDupItems - 1) / kDupItems);
+    scan_duplicate_kernel<<<dup_blocks, kBinThreads, 0, stream>>>(dp);
     GS_CHECK_LAUNCH();
     mark_stage(3, stream);
     for (int pass = 0; pass < P; ++pass) {
