@@ -183,6 +183,7 @@ static __global__ void __launch_bounds__(kBinThreads) bin_prepare_kernel(BinPara
 struct DupParams {
   int tiles_x;
   int n_tile_passes;
+  int runs;               // runs of kBinThreads Gaussians per CTA, 1..kDupRuns
   int tile_shift[4];      // digit bit offset of each tile-sort pass
   unsigned tile_mask[4];  // digit mask of each tile-sort pass
   const int* n_visible;
@@ -199,17 +200,23 @@ struct DupParams {
 
 // Exclusive scan of the tile counts in depth order and duplication of each Gaussian into
 // one (tile id, Gaussian index) pair per covered tile, row-major over its rectangle
-// (the order of csrc/forward/rasterize.cu:124-135). A CTA takes kDupRuns consecutive runs of
-// kBinThreads Gaussians: one look-back per CTA over a quarter as many CTAs as runs keeps the
-// decoupled look-back chain short (with one run per CTA the other warps spent most of the
-// kernel waiting at the barrier behind warp 0's walk), and the runs' rectangle loads are in
-// flight together. Within a run a warp's 32 Gaussians own a contiguous run of pairs, which the
+// (the order of csrc/forward/rasterize.cu:124-135). A CTA takes p.runs (1 to kDupRuns)
+// consecutive runs of kBinThreads Gaussians: one look-back per CTA over fewer CTAs keeps the
+// decoupled look-back chain short (with one run per CTA at 1M Gaussians the other warps spent
+// most of the kernel waiting at the barrier behind warp 0's walk), and the runs' rectangle loads
+// are in flight together. The host picks the runs so that the grid keeps at least four CTAs per
+// SM (dup_runs): few Gaussians with many pairs each need the CTAs more than a short chain. Within a run a warp's 32 Gaussians own a contiguous run of pairs, which the
 // warp writes 32 at a time: lanes where a Gaussian's pairs start in the current window record
 // their lane in a per-warp table and the window's start positions are OR-reduced into one
 // mask; pair lane q takes the Gaussian of the highest start at or below q (or the one carried
 // from the previous window) and fetches its rectangle by shuffle.
-constexpr int kDupRuns = 4;
-constexpr int kDupItems = kBinThreads * kDupRuns;  // Gaussians per CTA
+constexpr int kDupRuns = 4;  // most runs per CTA
+
+// Runs per duplication CTA for N Gaussians on `sms` SMs: as many as keep >= 4 CTAs per SM.
+inline int dup_runs(long long N, int sms) {
+  const long long r = N / ((long long)kBinThreads * 4 * sms);
+  return (int)(r < 1 ? 1 : (r > kDupRuns ? kDupRuns : r));
+}
 
 static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupParams p) {
   __shared__ unsigned s_tile, s_prefix;
@@ -220,7 +227,8 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
   constexpr unsigned kFull = 0xffffffffu;
   if ((long long)(*p.pair_count) > p.pair_capacity) return;
   const int nv = *p.n_visible;
-  const int num_tiles = (nv + kDupItems - 1) / kDupItems;
+  const int items = kBinThreads * p.runs;  // Gaussians per CTA
+  const int num_tiles = (nv + items - 1) / items;
   if (tid == 0) s_tile = atomicAdd(p.ticket, 1u);
   for (int k = tid; k < 4 * 256; k += kBinThreads) (&s_hist[0][0])[k] = 0u;
   __syncthreads();
@@ -230,21 +238,26 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
   uint2 pr[kDupRuns];
 #pragma unroll
   for (int r = 0; r < kDupRuns; ++r) {
-    const int j = tile * kDupItems + r * kBinThreads + tid;
-    gid[r] = j < nv ? p.sorted_gids[j] : 0u;
+    const int j = tile * items + r * kBinThreads + tid;
+    gid[r] = r < p.runs && j < nv ? p.sorted_gids[j] : 0u;
   }
 #pragma unroll
   for (int r = 0; r < kDupRuns; ++r) {
-    const int j = tile * kDupItems + r * kBinThreads + tid;
-    pr[r] = j < nv ? p.rects[gid[r]] : make_uint2(0u, 0u);
-    count[r] = j < nv ? rect_count(unpack_rect(pr[r])) : 0u;
+    const int j = tile * items + r * kBinThreads + tid;
+    const bool ok = r < p.runs && j < nv;
+    pr[r] = ok ? p.rects[gid[r]] : make_uint2(0u, 0u);
+    count[r] = ok ? rect_count(unpack_rect(pr[r])) : 0u;
   }
   // per run: each thread's exclusive offset within its run, and the run's total
   unsigned excl[kDupRuns], run_pairs[kDupRuns], tile_pairs = 0;
 #pragma unroll
   for (int r = 0; r < kDupRuns; ++r) {
-    excl[r] = block_exclusive_scan(count[r], s_scan, &run_pairs[r]);
-    tile_pairs += run_pairs[r];
+    excl[r] = 0u;
+    run_pairs[r] = 0u;
+    if (r < p.runs) {  // uniform over the CTA
+      excl[r] = block_exclusive_scan(count[r], s_scan, &run_pairs[r]);
+      tile_pairs += run_pairs[r];
+    }
   }
   if (tid == 0)
     st_relaxed(p.status + tile, (tile == 0 ? kFlagPrefix : kFlagAggregate) | tile_pairs);
@@ -267,6 +280,7 @@ static __global__ void __launch_bounds__(kBinThreads) scan_duplicate_kernel(DupP
   unsigned base = s_prefix;  // first pair of the current run
 #pragma unroll
   for (int r = 0; r < kDupRuns; ++r) {
+    if (r >= p.runs) break;  // uniform over the CTA
     // this warp's run of pairs: [w_first, w_first + w_total) of the run's
     const unsigned w_first = __shfl_sync(kFull, excl[r], 0);
     const unsigned w_total = __shfl_sync(kFull, excl[r] + count[r], 31) - w_first;

@@ -182,7 +182,9 @@ int launch_sort_and_blend(const RasterLayout& L, int N, int H, int W, char* ws,
     dp.tile_keys = tk[0];
     dp.tile_vals = tv[0];
     dp.tile_hist = reinterpret_cast<unsigned*>(ws + L.tile_hist);
-    const unsigned dup_blocks = (unsigned)(((long long)N + kDupItems - 1) / kDupItems);
+    dp.runs = dup_runs(N, sm_count());
+    const long long dup_items = (long long)kBinThreads * dp.runs;
+    const unsigned dup_blocks = (unsigned)(((long long)N + dup_items - 1) / dup_items);
     scan_duplicate_kernel<<<dup_blocks, kBinThreads, 0, stream>>>(dp);
     GS_CHECK_LAUNCH();
     mark_stage(3, stream);

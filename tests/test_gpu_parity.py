@@ -214,6 +214,27 @@ def test_matches_reference_live_large(crc, cuda_device):
         assert_grad_close(np32(a), np32(b), what)
 
 
+def test_matches_reference_live_many_tiles(crc, cuda_device):
+    """2560x1600 (16,000 tiles: 14-bit tile ids, two tile-sort passes of 8 and 6 bits, more tiles
+    than the tile-order kernel holds in registers in one chunk): 100k clustered Gaussians
+    through both the reference's kernels and ours, sorted order, ranges and image bit for bit."""
+    from gs3d_b200 import scenes
+
+    ref = _ref_module()
+    sc = scenes.config2(7, n=100_000)
+    view = scenes.pinhole((0.0, 0.0, 8.0), 2560, 1600, 2000.0)
+    out = gpu_forward(crc, sc, view, cuda_device)
+    H, W = view.height, view.width
+    r_img, r_ids, r_ranges, r_T, r_nc = ref.rasterize(
+        sc.N, out["depths"], out["mean2d"], out["cov2d"], out["colors"], out["alpha"], H, W)
+    assert out["tile_ranges"].shape[0] == 16_000
+    assert torch.equal(r_ids, out["sorted_ids"])
+    assert torch.equal(r_ranges, out["tile_ranges"])
+    assert torch.equal(r_nc, out["n_contrib"])
+    assert torch.equal(r_T, out["final_T"])
+    assert torch.equal(r_img, out["img"])
+
+
 # ---- edge cases ------------------------------------------------------------------------------
 def test_all_culled_scene(crc, cuda_device):
     from gs3d_b200 import scenes
