@@ -52,7 +52,15 @@ static_assert(kSsimBoxOff + kSsimInW <= kSsimBoxW && (kSsimBoxOff + kSsimR) % 4 
 constexpr unsigned kSsimBoxBytes = 3u * kSsimInH * kSsimBoxW * sizeof(float);
 constexpr unsigned long long kCopyWaitNs = 1000000000ull;  // 1 s for a tile copy to land
 
-__constant__ float c_gauss[kSsimTaps];
+// The 11-tap Gaussian window (sigma 1.5, normalised in double, each weight rounded to float) as
+// literals, so that the blurs' FMAs take them as immediates (with the window in constant memory
+// the compiler kept the weights in registers: the SSIM backward went from 96 to 77 registers
+// with literals). check_gauss compares them with the formula on the host.
+__host__ __device__ constexpr float gauss_w(int t) {
+  const int d = t < 5 ? t : 10 - t;
+  return d == 0 ? 0x1.0d956cp-10f : d == 1 ? 0x1.f1fe02p-8f : d == 2 ? 0x1.26eb18p-5f
+       : d == 3 ? 0x1.bff0fep-4f : d == 4 ? 0x1.b43c4p-3f : 0x1.106562p-2f;
+}
 
 // One channel at a time: its input planes and the horizontal blurs of its 5 moments.
 struct SsimForwardSmem {
@@ -76,7 +84,7 @@ __device__ __forceinline__ void blur_run(const float (&in)[kSsimWin], float (&ou
   for (int o = 0; o < kSsimRun; ++o) {
     float v = 0.f;
 #pragma unroll
-    for (int t = 0; t < kSsimTaps; ++t) v += c_gauss[t] * in[o + t];
+    for (int t = 0; t < kSsimTaps; ++t) v += gauss_w(t) * in[o + t];
     out[o] = v;
   }
 }
@@ -396,23 +404,21 @@ __global__ void __launch_bounds__(kSsimThreads, 5) ssim_backward_kernel(
   }
 }
 
-// The window lives in per-device constant memory; it is uploaded once per device.
-static int g_gauss_ready[64] = {};
-
-static int ensure_gauss() {
-  int dev = 0;
-  GS_CUDA(cudaGetDevice(&dev));
-  GS_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
-  if (g_gauss_ready[dev]) return GS_OK;
-  float w[kSsimTaps];
-  double sum = 0.0;
-  for (int k = 0; k < kSsimTaps; ++k) {
-    const double x = k - (kSsimTaps - 1) / 2.0;
-    sum += w[k] = (float)exp(-(x * x) / (2.0 * 1.5 * 1.5));
-  }
-  for (int k = 0; k < kSsimTaps; ++k) w[k] = (float)(w[k] / sum);
-  GS_CUDA(cudaMemcpyToSymbol(c_gauss, w, sizeof(w)));
-  g_gauss_ready[dev] = 1;
+// The window's literals (gauss_w) against its formula: exp(-x^2 / (2 sigma^2)) in double for
+// x = -5..5, each rounded to float, normalised by their double sum and rounded again.
+static int check_gauss() {
+  static const bool ok = [] {
+    float w[kSsimTaps];
+    double sum = 0.0;
+    for (int k = 0; k < kSsimTaps; ++k) {
+      const double x = k - (kSsimTaps - 1) / 2.0;
+      sum += w[k] = (float)exp(-(x * x) / (2.0 * 1.5 * 1.5));
+    }
+    bool same = true;
+    for (int k = 0; k < kSsimTaps; ++k) same = same && (float)(w[k] / sum) == gauss_w(k);
+    return same;
+  }();
+  GS_REQUIRE(ok, "SSIM window literals differ from the Gaussian formula");
   return GS_OK;
 }
 
@@ -453,7 +459,7 @@ extern "C" int gs_l1_ssim_forward(int H, int W, const float* img, const float* t
              "SSIM needs images of at least 11 x 11 pixels (an 11 x 11 window inside the image)");
   GS_REQUIRE(img && target && workspace && loss, "null pointer");
   GS_REQUIRE(workspace_bytes >= gs_l1_ssim_workspace_size(H, W), "workspace too small");
-  const int rc = ensure_gauss();
+  const int rc = check_gauss();
   if (rc != GS_OK) return rc;
   float* maps = maps_of(workspace);
   double* partials = partials_of(workspace, H, W);
@@ -481,7 +487,7 @@ extern "C" int gs_l1_ssim_backward(int H, int W, const float* img, const float* 
              "SSIM needs images of at least 11 x 11 pixels (an 11 x 11 window inside the image)");
   GS_REQUIRE(img && target && workspace && grad_loss && grad_img, "null pointer");
   GS_REQUIRE(workspace_bytes >= gs_l1_ssim_workspace_size(H, W), "workspace too small");
-  const int rc = ensure_gauss();
+  const int rc = check_gauss();
   if (rc != GS_OK) return rc;
   const dim3 grid((W + kSsimTW - 1) / kSsimTW, (H + kSsimTH - 1) / kSsimTH);
   const size_t smem = sizeof(SsimBackwardSmem);
