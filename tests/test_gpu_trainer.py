@@ -122,3 +122,42 @@ def test_direct_step_renders_overflowed_views_again(cuda_device):
     assert_grad_close(got[True][1], got[False][1], "bucket")
     assert_grad_close(got[True][2], got[False][2], "max statistic")
     assert crc.device_error_bits() == 0
+
+
+def test_per_gaussian_backward_split_has_the_same_bits(cuda_device):
+    """The combined per-Gaussian backward over views [0, 1, 2] in one call, and over [0, 1] and
+    then [2] accumulating, give the same gradients and statistics bit for bit on the same blend
+    sums: the kernel adds the views in list order after the buffers' values."""
+    from custom_rasterizer_cuda.render import (backward_workspace, render_backward_blend,
+                                               render_backward_views, render_forward)
+
+    sc, views, _ = _small_setup()
+    dev = cuda_device
+    mu, q, s, al, A, kj = (p.to(dev).contiguous() for p in sc.params())
+    op = torch.sigmoid(al).reshape(-1).contiguous()
+    g = torch.Generator("cpu").manual_seed(3)
+    entries = []
+    for v in views:
+        R, t = v.R.to(dev).contiguous(), v.T.to(dev).contiguous()
+        cam = (-(R.T @ t)).reshape(3).contiguous()
+        _, _, st = render_forward(mu, q, s, op, A, kj, R, t, cam, v.fx, v.fy, v.cx, v.cy,
+                                  v.height, v.width)
+        ws = backward_workspace(sc.N, dev)
+        render_backward_blend(st, torch.rand(v.height, v.width, 3, generator=g).to(dev), sc.N, ws)
+        entries.append((ws, R, t, cam, v.fx, v.fy, v.cx, v.cy, v.width / 2.0, v.height / 2.0))
+
+    def run(groups):
+        out = tuple(torch.zeros_like(x) for x in (mu, q, s, op, A, kj))
+        stats = tuple(torch.zeros(sc.N, device=dev) for _ in range(3))
+        for i, grp in enumerate(groups):
+            render_backward_views(grp, mu, q, s, A, kj, out, accumulate=i > 0, stats=stats)
+        torch.cuda.synchronize()
+        return [x.cpu() for x in out + stats]
+
+    one = run([entries])
+    split = run([entries[:2], entries[2:]])
+    names = ("mu", "q", "s", "opacity", "albedo", "k_j", "norm_sum", "count", "norm_max")
+    for a, b, what in zip(split, one, names):
+        assert torch.equal(a, b), what
+    assert float(one[6].abs().sum()) > 0
+
